@@ -1,0 +1,414 @@
+"""Benchmark of the GDN hot path on B200 — prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill_varlen|prefill_long]
+                    [--impl ours|reference]
+
+Workloads (seeded synthetic inputs with the benchmark configurations' shapes and
+distributions; the reference's official trace dataset is not available):
+
+* ``decode`` (default, the headline): B=256 sequences per GPU, 16 q/k heads,
+  32 v heads, D=128, fp32 state [256,32,128,128] (512 MiB read + 512 MiB
+  written per step). Metric: state GB/s = 2*B*HV*D*D*4 / t_step, the
+  reference's own formula (gdn/scripts/bench_cuda_real.py:556, :589). A step
+  feeds the previous step's new_state back in (a real decode loop); the state
+  is larger than L2 so no flush is needed.
+* ``prefill_varlen``: 8 sequences, lengths ~U[512,4096] (seed 0), int32 cu_seqlens,
+  initial state ~N(0,0.02). Metric: tokens/s.
+* ``prefill_long``: 4 sequences x 32768 tokens per GPU, zero initial state. Metric: tokens/s.
+
+Multi-GPU (torchrun, one process per GPU): every rank owns its own batch slice
+(weak scaling, no data-path collective); the step time is the max over ranks.
+
+``--impl reference`` times the reference's CPU implementation of the same path
+(the oracle restatement of the reference's PyTorch baseline, run on the host
+cores with all threads) on a bounded sample of the workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+HQ, HV, D = 16, 32, 128
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+L2_BYTES = 126 * 2 ** 20
+
+
+# ----------------------------------------------------------------------------- env / dist
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(
+            d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def ncu_traffic(key: str):
+    """DRAM bytes per launch of the dominant kernel, from a committed ncu summary
+    (a line ``traffic_per_launch[<key>] = <bytes>`` in profiles/*.md)."""
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        m = re.search(rf"traffic_per_launch\[{re.escape(key)}\]\s*=\s*([0-9.eE+]+)", f.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.file = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            sel = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", sel, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = [r.split(", ") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], None, set()
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, val in zip(self.NAMES, r[5:9]):
+                if val.strip() == "Active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workloads
+def decode_workload(device, seed):
+    from flashinfer_bench_tma_thrust_b200 import workloads as W
+    B = 256
+    x = W.decode_inputs(B, seed=seed, gen_device=device, device=device)
+    state_bytes = 2 * B * HV * D * D * 4
+    io_bytes = (2 * B * HQ * D + B * HV * D) * 2 + B * HV * D * 2 + 2 * B * HV * 2
+    return x, {"B": B, "state_bytes": state_bytes, "alg_bytes": state_bytes + io_bytes}
+
+
+def prefill_lengths(workload):
+    from flashinfer_bench_tma_thrust_b200 import workloads as W
+    if workload == "prefill_varlen":
+        return W.varlen_lengths(seed=0), True
+    return [32768] * 4, False
+
+
+def time_steps(step, K, W, device, world):
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(K):
+        step()
+    end.record()
+    end.synchronize()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    return ms
+
+
+def kernel_launch_ms(step, n, device):
+    """Average device time of one step's launch, CUDA events on the launching stream."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n)]
+    torch.cuda.synchronize(device)
+    for s, e in evs:
+        s.record()
+        step()
+        e.record()
+    torch.cuda.synchronize(device)
+    return statistics.mean(s.elapsed_time(e) for s, e in evs)
+
+
+def cpu_decode_baseline(seconds=10.0, sample_B=16):
+    """Oracle (restated reference PyTorch decode) on the host cores, on a sample of the
+    B=256 workload's sequences per step."""
+    from flashinfer_bench_tma_thrust_b200 import workloads as W
+    from oracle import gdn_oracle
+    x = W.decode_inputs(256, seed=0)
+    sl = [t[:sample_B] if isinstance(t, torch.Tensor) and t.dim() > 1 else t for t in x.args()]
+    gdn_oracle.decode(*sl)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        gdn_oracle.decode(*sl)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 3:
+            break
+    sb = 2 * sample_B * HV * D * D * 4
+    return {"value": sb * n / el / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{sample_B} of the 256 sequences per step, {n} steps in {el:.1f} s, "
+                      f"torch CPU fp32, {torch.get_num_threads()} threads of "
+                      f"{os.cpu_count()} cpus"}
+
+
+def cpu_prefill_baseline(lengths, seconds=10.0, tokens_per_seq=64):
+    from flashinfer_bench_tma_thrust_b200 import workloads as W
+    from oracle import gdn_oracle
+    sub = [min(l, tokens_per_seq) for l in lengths]
+    x = W.prefill_inputs(sub, seed=0)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        gdn_oracle.prefill(*x.args())
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 1:
+            break
+    return {"value": sum(sub) * n / el, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"first {tokens_per_seq} tokens of each of the {len(lengths)} sequences "
+                      f"({sum(sub)} tokens) per step, {n} steps in {el:.1f} s, torch CPU fp32, "
+                      f"{torch.get_num_threads()} threads of {os.cpu_count()} cpus"}
+
+
+# ----------------------------------------------------------------------------- arms
+def run_ours(args, world, rank, local):
+    from flashinfer_bench_tma_thrust_b200 import decode, prefill
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    hbm, bf16, bf16_sus, peak_src = peaks()
+    K, Wm = args.steps, args.warmup
+    result = {"n_gpus": world, "steps": K, "warmup": Wm, "higher_is_better": True,
+              "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
+    if args.workload == "decode":
+        x, info = decode_workload(device, seed=1000 + rank)
+        B = info["B"]
+        holder = {"s": x.state.clone()}
+
+        def step():
+            _, ns = decode.kernel(x.q, x.k, x.v, holder["s"], x.A_log, x.a, x.dt_bias, x.b,
+                                  x.scale)
+            holder["s"] = ns
+
+        sampler = ClockSampler(device)
+        ms = time_steps(step, K, Wm, device, world)
+        clocks = sampler.stop()
+        ms_step = ms / K
+        value = world * info["state_bytes"] / (ms_step * 1e-3) / 1e9
+        k_ms = kernel_launch_ms(step, 50, device)
+        achieved = info["alg_bytes"] / (k_ms * 1e-3) / 1e9
+        traffic = ncu_traffic("decode_b256")
+        result.update({
+            "metric": "GDN decode state GB/s (2*B*HV*D*D*4 / step time)",
+            "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms_step, 5),
+            "dtype": "f32",
+            "pct_of_8TBps": round(100.0 * value / world / 8000.0, 2),
+            "config": {"workload": f"gdn_decode B={B}/GPU, 16 q/k heads, 32 v heads, D=128, "
+                                   "fp32 k-last state, bf16 q/k/v/a/b",
+                       "global_batch": B * world, "parallelism": f"sequence-sharded x{world}",
+                       "l2": "state (512 MiB in + 512 MiB out per GPU) larger than L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                         "peak_source": peak_src, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "traffic": traffic,
+                         "alg_bytes_per_launch": info["alg_bytes"],
+                         "kernel_ms": round(k_ms, 5)},
+            "clocks": clocks, "gpu_launches": K,
+        })
+        if not args.no_e2e:
+            result["e2e"] = decode_e2e(x, info, device, world, min(K, 10), min(Wm, 3))
+        if world == 1 and rank == 0 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_decode_baseline()
+    else:
+        lengths, with_state = prefill_lengths(args.workload)
+        from flashinfer_bench_tma_thrust_b200 import workloads as W
+        x = W.prefill_inputs(lengths, seed=2000 + rank, gen_device=device, device=device,
+                             with_state=with_state)
+        T = sum(lengths)
+
+        def step():
+            prefill.kernel(*x.args())
+
+        sampler = ClockSampler(device)
+        ms = time_steps(step, K, Wm, device, world)
+        clocks = sampler.stop()
+        ms_step = ms / K
+        value = world * T / (ms_step * 1e-3)
+        flop_per_token = HV * (6 * D * D + 10 * 64 * D + (2 * 64 * 64) // 3)
+        k_ms = kernel_launch_ms(step, 5, device)
+        achieved = T * flop_per_token / (k_ms * 1e-3) / 1e12
+        result.update({
+            "metric": "GDN prefill tokens/s", "value": round(value, 1), "unit": "tokens/s",
+            "ms_per_step": round(ms_step, 4), "dtype": "f32 state, bf16 tensor-core operands",
+            "config": {"workload": f"gdn_prefill {args.workload}: lengths {lengths[:8]}"
+                                   f"{'...' if len(lengths) > 8 else ''} (T={T}/GPU), 16 q/k "
+                                   "heads, 32 v heads, D=128, chunk 64",
+                       "global_tokens": T * world, "parallelism": f"sequence-sharded x{world}",
+                       "l2": "inputs (q/k/v >= 100 MB per GPU) larger than L2; no flush"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16_sus,
+                         "peak_source": peak_src + " (sustained bf16)", "unit": "TFLOP/s",
+                         "frac": round(achieved / bf16_sus, 4),
+                         "traffic": ncu_traffic(args.workload),
+                         "flop_per_token": flop_per_token, "kernel_ms": round(k_ms, 4)},
+            "clocks": clocks, "gpu_launches": K * prefill.launches_per_call(),
+        })
+        if world == 1 and rank == 0 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_prefill_baseline(lengths)
+    return result
+
+
+def decode_e2e(x, info, device, world, K, Wm):
+    """Same metric through the public API with host buffers: every step copies its
+    inputs from pinned host memory and reads output + new state back."""
+    from flashinfer_bench_tma_thrust_b200 import decode
+    host = [t.cpu().pin_memory() if isinstance(t, torch.Tensor) else t for t in x.args()]
+    B = info["B"]
+    out_h = torch.empty(B, 1, HV, D, dtype=torch.bfloat16).pin_memory()
+    ns_h = torch.empty(B, HV, D, D, dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host if isinstance(t, torch.Tensor))
+    d2h = out_h.numel() * 2 + ns_h.numel() * 4
+
+    def step():
+        dev_args = [t.to(device, non_blocking=True) if isinstance(t, torch.Tensor) else t
+                    for t in host]
+        out, ns = decode.kernel(*dev_args)
+        out_h.copy_(out, non_blocking=True)
+        ns_h.copy_(ns, non_blocking=True)
+
+    ms = time_steps(step, K, Wm, device, world)
+    return {"value": round(world * info["state_bytes"] / (ms / K * 1e-3) / 1e9, 3),
+            "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": K,
+            "ms_per_step": round(ms / K, 3)}
+
+
+def run_reference(args):
+    """Reference arm: the reference's PyTorch path (restated in oracle/) on the host CPU."""
+    from flashinfer_bench_tma_thrust_b200 import workloads as W
+    from oracle import gdn_oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    K, Wm = args.steps, args.warmup
+    if args.workload == "decode":
+        sample_B = 4
+        x = W.decode_inputs(256, seed=1000)
+        sl = [t[:sample_B] if isinstance(t, torch.Tensor) and t.dim() > 1 else t
+              for t in x.args()]
+        fn = lambda: gdn_oracle.decode(*sl)  # noqa: E731
+        units = 2 * sample_B * HV * D * D * 4
+        metric, unit = "GDN decode state GB/s (2*B*HV*D*D*4 / step time)", "GB/s"
+        scale = 1e-9
+        sample = f"{sample_B} of the 256 sequences of the decode workload per step"
+        cfg = "gdn_decode B=256/GPU, 16 q/k heads, 32 v heads, D=128, fp32 k-last state"
+    else:
+        lengths, with_state = prefill_lengths(args.workload)
+        sub = [min(l, 16) for l in lengths]
+        x = W.prefill_inputs(sub, seed=2000, with_state=with_state)
+        fn = lambda: gdn_oracle.prefill(*x.args())  # noqa: E731
+        units = sum(sub)
+        metric, unit, scale = "GDN prefill tokens/s", "tokens/s", 1.0
+        sample = f"first 16 tokens of each of the {len(lengths)} sequences per step"
+        cfg = f"gdn_prefill {args.workload}: lengths {lengths[:8]}, 16 q/k heads, 32 v heads"
+    for _ in range(Wm):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        fn()
+    el = time.perf_counter() - t0
+    value = units * K / el * scale
+    cores = torch.get_num_threads()
+    line = {"impl": "reference", "metric": metric, "value": round(value, 4), "unit": unit,
+            "n_gpus": args.gpus, "steps": K, "warmup": Wm, "ms_per_step": round(el / K * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": cfg},
+            "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": cores,
+                             "kind": "port",
+                             "sample": f"{sample}; torch CPU fp32 restatement of the reference "
+                                       f"PyTorch baseline, {cores} threads"},
+            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill_varlen", "prefill_long"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 2000 if args.workload == "decode" else 20
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args)
+        return
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+    try:
+        res = run_ours(args, world, rank, local)
+        if rank == 0:
+            line = {"metric": res.pop("metric"), "value": res.pop("value"), "unit": res.pop("unit")}
+            line.update(res)
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

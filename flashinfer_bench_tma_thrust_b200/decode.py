@@ -1,0 +1,84 @@
+"""GDN single-token decode — drop-in for the reference's decode solution entry.
+
+``kernel(q, k, v, state, A_log, a, dt_bias, b, scale) -> (output, new_state)``
+has the signature of ``gdn/decode/solution/triton/kernel.py:85`` (selected by
+``gdn/decode/config.toml``: ``entry_point = "kernel.py::kernel"``) and the tensor
+contract of ``gdn/trace_definitions/gdn_decode_qk4_v8_d128_k_last.json``:
+
+    q, k     [B, 1, HQ, 128] bf16        v [B, 1, HV, 128] bf16
+    state    [B, HV, 128, 128] fp32 k-last, or None (zeros)
+    A_log    [HV] fp32    a [B, 1, HV] bf16/fp32    dt_bias [HV] fp32    b [B, 1, HV]
+    scale    float, None or 0.0 -> 1/sqrt(128)
+    returns  output [B, 1, HV, 128] bf16, new_state [B, HV, 128, 128] fp32
+
+Inputs are never modified (the reference clones the state,
+gdn/decode/baseline/triton/kernel.py:75). ``kernel_inplace`` is the
+serving-oriented variant that writes the new state over ``state``.
+All work runs in one launch of the sm_100a decode kernel on the current stream.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _checks as C
+from . import _lib
+
+
+def _launch(q, k, v, state, A_log, a, dt_bias, b, scale, out, new_state):
+    dev = q.device
+    B, T, HQ, D = q.shape
+    if T != 1:
+        raise ValueError(f"decode expects seq_len 1 (q.shape[1]), got {T}")
+    HV = v.shape[2]
+    C.check_heads(HQ, HV, D)
+    if k.shape != q.shape:
+        raise ValueError(f"k shape {tuple(k.shape)} != q shape {tuple(q.shape)}")
+    if tuple(v.shape) != (B, 1, HV, D):
+        raise ValueError(f"v must be [B,1,HV,{D}], got {tuple(v.shape)}")
+    for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a),
+                    ("dt_bias", dt_bias), ("b", b)):
+        C.require_cuda(name, t, dev)
+    if a.numel() != B * HV or b.numel() != B * HV:
+        raise ValueError("a and b must have B*HV elements ([B,1,HV])")
+    if A_log.numel() != HV or dt_bias.numel() != HV:
+        raise ValueError("A_log and dt_bias must have HV elements")
+    q_c, k_c, v_c = C.as_bf16("q", q), C.as_bf16("k", k), C.as_bf16("v", v)
+    A_c, A_t = C.as_gate("A_log", A_log)
+    a_c, a_t = C.as_gate("a", a)
+    d_c, d_t = C.as_gate("dt_bias", dt_bias)
+    b_c, b_t = C.as_gate("b", b)
+    s_c = None
+    if state is not None:
+        C.require_cuda("state", state, dev)
+        if tuple(state.shape) != (B, HV, D, D):
+            raise ValueError(f"state must be [B,HV,{D},{D}], got {tuple(state.shape)}")
+        s_c = state.float().contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.gdn_decode_fwd(
+            q_c.data_ptr(), k_c.data_ptr(), v_c.data_ptr(), C.ptr(s_c),
+            A_c.data_ptr(), A_t, a_c.data_ptr(), a_t, d_c.data_ptr(), d_t, b_c.data_ptr(), b_t,
+            C.resolve_scale(scale, D), out.data_ptr(), new_state.data_ptr(), B, HQ, HV, D,
+            C.stream_handle(dev))
+    _lib.check(rc, "gdn_decode_fwd")
+    return out, new_state
+
+
+def kernel(q, k, v, state, A_log, a, dt_bias, b, scale=None):
+    """Reference-compatible decode: returns freshly allocated (output, new_state)."""
+    B, _, _, D = q.shape
+    HV = v.shape[2]
+    out = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=q.device)
+    new_state = torch.empty(B, HV, D, D, dtype=torch.float32, device=q.device)
+    return _launch(q, k, v, state, A_log, a, dt_bias, b, scale, out, new_state)
+
+
+def kernel_inplace(q, k, v, state, A_log, a, dt_bias, b, scale=None, out=None):
+    """Decode that updates ``state`` (fp32, contiguous) in place; returns (output, state)."""
+    if state is None or state.dtype != torch.float32 or not state.is_contiguous():
+        raise ValueError("kernel_inplace needs a contiguous fp32 state tensor")
+    B, _, _, D = q.shape
+    HV = v.shape[2]
+    if out is None:
+        out = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=q.device)
+    return _launch(q, k, v, state, A_log, a, dt_bias, b, scale, out, state)

@@ -1,0 +1,110 @@
+"""GDN variable-length prefill — drop-in for the reference's prefill solution entry.
+
+``kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale) -> (output, new_state)``
+has the signature of ``gdn/prefill/solution/triton/kernel.py:272`` (selected by
+``gdn/prefill/config.toml``) and the tensor contract of
+``gdn/trace_definitions/gdn_prefill_qk4_v8_d128_k_last.json``:
+
+    q, k        [T, HQ, 128] bf16          v [T, HV, 128] bf16
+    state       [N, HV, 128, 128] fp32 k-last, or None (zeros)
+    A_log       [HV] fp32    a, b [T, HV] bf16/fp32    dt_bias [HV] fp32
+    cu_seqlens  [N+1] int64 (definition) or int32 (reference tests)
+    returns     output [T, HV, 128] bf16, new_state [N, HV, 128, 128] fp32
+
+A sequence with cu_seqlens[n+1] <= cu_seqlens[n] passes its state through
+(gdn/prefill/baseline/triton/kernel.py:68-71). Inputs are never modified.
+
+``kernel_recurrent`` runs the token-sequential kernel (the independent
+cross-check); ``kernel`` runs the chunked tensor-core kernel.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _checks as C
+from . import _lib
+
+
+class _Prepared:
+    __slots__ = ("dev", "T", "N", "HQ", "HV", "D", "q", "k", "v", "state", "A", "A_t", "a",
+                 "a_t", "d", "d_t", "b", "b_t", "cu", "cu_t", "scale")
+
+
+def prepare(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale) -> _Prepared:
+    """Validate shapes/dtypes/devices and make every tensor contiguous."""
+    P = _Prepared()
+    dev = q.device
+    if q.dim() != 3:
+        raise ValueError(f"q must be [T, HQ, D], got {tuple(q.shape)}")
+    T, HQ, D = q.shape
+    if v.dim() != 3 or v.shape[0] != T or v.shape[2] != D:
+        raise ValueError(f"v must be [T, HV, {D}], got {tuple(v.shape)}")
+    HV = v.shape[1]
+    C.check_heads(HQ, HV, D)
+    if k.shape != q.shape:
+        raise ValueError(f"k shape {tuple(k.shape)} != q shape {tuple(q.shape)}")
+    for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a),
+                    ("dt_bias", dt_bias), ("b", b), ("cu_seqlens", cu_seqlens)):
+        C.require_cuda(name, t, dev)
+    if cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1:
+        raise ValueError("cu_seqlens must be a 1-D tensor of length num_seqs + 1")
+    N = cu_seqlens.numel() - 1
+    if a.numel() != T * HV or b.numel() != T * HV:
+        raise ValueError("a and b must be [T, HV]")
+    if A_log.numel() != HV or dt_bias.numel() != HV:
+        raise ValueError("A_log and dt_bias must have HV elements")
+    P.dev, P.T, P.N, P.HQ, P.HV, P.D = dev, T, N, HQ, HV, D
+    P.q, P.k, P.v = C.as_bf16("q", q), C.as_bf16("k", k), C.as_bf16("v", v)
+    P.A, P.A_t = C.as_gate("A_log", A_log)
+    P.a, P.a_t = C.as_gate("a", a)
+    P.d, P.d_t = C.as_gate("dt_bias", dt_bias)
+    P.b, P.b_t = C.as_gate("b", b)
+    P.cu, P.cu_t = C.as_index("cu_seqlens", cu_seqlens)
+    P.state = None
+    if state is not None:
+        C.require_cuda("state", state, dev)
+        if tuple(state.shape) != (N, HV, D, D):
+            raise ValueError(f"state must be [N,HV,{D},{D}], got {tuple(state.shape)}")
+        P.state = state.float().contiguous()
+    P.scale = C.resolve_scale(scale, D)
+    return P
+
+
+def _alloc_outputs(P: _Prepared):
+    out = torch.empty(P.T, P.HV, P.D, dtype=torch.bfloat16, device=P.dev)
+    new_state = torch.empty(P.N, P.HV, P.D, P.D, dtype=torch.float32, device=P.dev)
+    return out, new_state
+
+
+def _ptr0(t):
+    # zero-element tensors may report a null data_ptr; the ABI accepts that when T == 0
+    return t.data_ptr() if t.numel() else None
+
+
+def run_recurrent(P: _Prepared, out, new_state):
+    lib = _lib.load()
+    with torch.cuda.device(P.dev):
+        rc = lib.gdn_prefill_recurrent_fwd(
+            _ptr0(P.q), _ptr0(P.k), _ptr0(P.v), C.ptr(P.state),
+            P.A.data_ptr(), P.A_t, _ptr0(P.a), P.a_t, P.d.data_ptr(), P.d_t, _ptr0(P.b), P.b_t,
+            P.cu.data_ptr(), P.cu_t, P.scale, _ptr0(out), _ptr0(new_state),
+            P.T, P.N, P.HQ, P.HV, P.D, C.stream_handle(P.dev))
+    _lib.check(rc, "gdn_prefill_recurrent_fwd")
+    return out, new_state
+
+
+def kernel_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
+    """Token-sequential prefill (one launch of the SIMT recurrent kernel)."""
+    P = prepare(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+    out, new_state = _alloc_outputs(P)
+    return run_recurrent(P, out, new_state)
+
+
+def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
+    """Reference-compatible prefill entry point."""
+    return kernel_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+
+
+def launches_per_call() -> int:
+    """Kernel launches one ``kernel()`` call makes (reported by the benchmark)."""
+    return 1

@@ -1,0 +1,116 @@
+/*
+ * gdn_b200.h — C ABI of the B200 (sm_100a) Gated Delta Net operators.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed
+ * as void*, launches asynchronously on that stream and returns a status code
+ * (GDN_OK or a negative GDN_ERR_*). No exception crosses this boundary and no
+ * entry point synchronises the host with the device.
+ *
+ * Tensors are dense row-major (C-contiguous). Shapes use the names of the
+ * reference's trace definitions (gdn/trace_definitions/gdn_{decode,prefill}_
+ * qk4_v8_d128_k_last.json): q/k [.., HQ, D], v [.., HV, D], state k-last
+ * [.., HV, V=D, K=D] fp32. D must be 128 and HV a multiple of HQ (GVA: v-head h
+ * reads q/k head h / (HV/HQ)).
+ *
+ * The reference binds its kernels through torch-typed pybind wrappers
+ * (gdn/decode/solution/cuda/kernel.py:295-364) and through void C launchers
+ * with raw pointers (gdn/gdn_kernels.cu:26-170); these functions replace both
+ * with one status-returning C interface.
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define GDN_OK 0
+#define GDN_ERR_INVALID_ARG (-1)      /* null pointer where one is required, negative size */
+#define GDN_ERR_UNSUPPORTED_SHAPE (-2)/* D != 128, HV not a multiple of HQ, ... */
+#define GDN_ERR_UNSUPPORTED_DTYPE (-3)/* dtype code not accepted for that argument */
+#define GDN_ERR_CUDA (-4)             /* a CUDA runtime call or a kernel launch failed */
+#define GDN_ERR_WORKSPACE (-5)        /* workspace null or smaller than required */
+#define GDN_ERR_DEVICE (-6)           /* device is not sm_100 class */
+
+/* Element type codes for arguments that accept more than one type. */
+#define GDN_DTYPE_F32 0
+#define GDN_DTYPE_BF16 1
+#define GDN_DTYPE_I32 2
+#define GDN_DTYPE_I64 3
+
+/* Version of this ABI; bumped on any signature change. */
+GDN_API int gdn_abi_version(void);
+
+/* Human-readable text for a status code (static storage). */
+GDN_API const char* gdn_status_string(int status);
+
+/*
+ * Single-token decode: one recurrent step for B sequences.
+ *
+ * Replaces the solution entry kernel(q,k,v,state,A_log,a,dt_bias,b,scale)
+ * of gdn/decode/solution/triton/kernel.py:85-135 (same math as the PyTorch
+ * baseline gdn/decode/baseline/triton/kernel.py:27-100).
+ *
+ *   q, k      bf16 [B, HQ, D]       (the reference's [B, 1, HQ, D])
+ *   v         bf16 [B, HV, D]
+ *   state     fp32 [B, HV, D, D] k-last, or NULL for a zero initial state
+ *   A_log     [HV]    dtype A_log_dtype   (F32 or BF16)
+ *   a         [B, HV] dtype a_dtype       (F32 or BF16)
+ *   dt_bias   [HV]    dtype dt_bias_dtype (F32 or BF16)
+ *   b         [B, HV] dtype b_dtype       (F32 or BF16)
+ *   scale     output scale; <= 0 selects 1/sqrt(D) (reference: None or 0.0)
+ *   out       bf16 [B, HV, D]
+ *   new_state fp32 [B, HV, D, D] k-last. May alias `state` (in-place update):
+ *             every element is read and then written by the same thread.
+ *
+ * B == 0 is a no-op returning GDN_OK. Offsets are 64-bit (B up to 2^31-1).
+ */
+GDN_API int gdn_decode_fwd(const void* q, const void* k, const void* v, const float* state,
+                   const void* A_log, int A_log_dtype, const void* a, int a_dtype,
+                   const void* dt_bias, int dt_bias_dtype, const void* b, int b_dtype,
+                   float scale, void* out, float* new_state, int64_t B, int32_t HQ,
+                   int32_t HV, int32_t D, void* stream);
+
+/*
+ * Variable-length prefill over cu_seqlens-packed sequences, token-sequential
+ * recurrence (one thread block per sequence, v-head and 32-row V tile, the
+ * state tile held in registers across the whole sequence).
+ *
+ * Same semantics as gdn/prefill/baseline/triton/kernel.py:18-100; the
+ * structure of gdn/prefill/solution/triton/kernel.py:99-209. Kept as an
+ * independent second implementation to cross-check the chunked kernel at
+ * sizes the CPU oracle cannot reach.
+ *
+ *   q, k        bf16 [T, HQ, D];  v bf16 [T, HV, D]
+ *   state       fp32 [N, HV, D, D] k-last or NULL (zeros)
+ *   a, b        [T, HV] (F32 or BF16);  A_log, dt_bias [HV] (F32 or BF16)
+ *   cu_seqlens  [N+1] int32 or int64 (cu_dtype), device memory
+ *   out         bf16 [T, HV, D];  new_state fp32 [N, HV, D, D]
+ *
+ * A sequence with end <= start copies its initial state through (zeros when
+ * state is NULL), as the reference does (baseline kernel.py:68-71). Token
+ * indices are clamped to [0, T] so a malformed cu_seqlens cannot read or write
+ * outside the buffers. new_state must not alias state.
+ */
+GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* v, const float* state,
+                              const void* A_log, int A_log_dtype, const void* a, int a_dtype,
+                              const void* dt_bias, int dt_bias_dtype, const void* b,
+                              int b_dtype, const void* cu_seqlens, int cu_dtype, float scale,
+                              void* out, float* new_state, int64_t T, int64_t N, int32_t HQ,
+                              int32_t HV, int32_t D, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

@@ -1,0 +1,84 @@
+"""Prefill parity on the GPU: chunked (kernel) and token-sequential (kernel_recurrent)
+sm_100a kernels through the C ABI vs the oracle and the reference's golden outputs."""
+import pytest
+import torch
+
+from flashinfer_bench_tma_thrust_b200 import prefill, workloads as W
+from golden import golden
+from oracle import gdn_oracle
+from parity import (PREFILL_STATE_ATOL, STATE_REL_FROB, assert_out_close, assert_state_close,
+                    to_dev)
+
+pytestmark = pytest.mark.gpu
+
+PRE_CASES = [c for c in golden.case_names() if c.startswith("pre_")]
+IMPLS = {"chunked": prefill.kernel, "recurrent": prefill.kernel_recurrent}
+
+
+@pytest.mark.parametrize("impl", sorted(IMPLS))
+@pytest.mark.parametrize("name", PRE_CASES)
+def test_prefill_matches_reference_golden(name, impl):
+    _, x, exp = golden.load_case(name)
+    out, ns = IMPLS[impl](*to_dev(x).args())
+    assert_out_close(out, exp["out"], name)
+    err, rel = golden.compare_state(ns, exp, atol=PREFILL_STATE_ATOL, rtol_frob=STATE_REL_FROB)
+    assert err <= PREFILL_STATE_ATOL and rel <= STATE_REL_FROB, (name, err, rel)
+
+
+LENGTHS = [
+    [1], [63], [64], [65], [128], [200, 0, 1, 64, 127],
+    [0, 0], [300, 17],
+]
+
+
+@pytest.mark.parametrize("impl", sorted(IMPLS))
+@pytest.mark.parametrize("lengths", LENGTHS, ids=lambda l: "-".join(map(str, l)))
+def test_prefill_full_heads_vs_oracle(lengths, impl):
+    x = W.prefill_inputs(lengths, seed=sum(lengths) + len(lengths))
+    ref_out, ref_ns = gdn_oracle.prefill(*x.args())
+    out, ns = IMPLS[impl](*to_dev(x).args())
+    assert out.shape == (sum(lengths), 32, 128) and ns.shape == (len(lengths), 32, 128, 128)
+    assert_out_close(out, ref_out, str(lengths))
+    assert_state_close(ns, ref_ns, PREFILL_STATE_ATOL, str(lengths))
+
+
+@pytest.mark.parametrize("impl", sorted(IMPLS))
+@pytest.mark.parametrize("dist", ["baseline", "reftest"])
+def test_prefill_no_state_int64_bf16_gates(impl, dist):
+    x = W.prefill_inputs([70, 5, 0, 130], HQ=4, HV=8, seed=3, dist=dist, with_state=False,
+                         cu_dtype=torch.int64, gate_dtype=torch.bfloat16)
+    ref_out, ref_ns = gdn_oracle.prefill(*x.args())
+    out, ns = IMPLS[impl](*to_dev(x).args())
+    assert_out_close(out, ref_out)
+    assert_state_close(ns, ref_ns, PREFILL_STATE_ATOL)
+    assert torch.count_nonzero(ns[2]) == 0  # empty sequence, no initial state -> zeros
+
+
+@pytest.mark.parametrize("impl", sorted(IMPLS))
+def test_prefill_empty_sequence_passthrough_exact(impl):
+    """Empty sequences copy their state through (reference threshold < 1e-6,
+    gdn/tests/test_correctness.py:506-514); here it must be bit-exact."""
+    x = to_dev(W.prefill_inputs([0, 9, 0], HQ=2, HV=4, seed=5))
+    s0 = x.state.clone()
+    out, ns = IMPLS[impl](*x.args())
+    assert torch.equal(ns[0], s0[0]) and torch.equal(ns[2], s0[2])
+    assert torch.equal(x.state, s0), "inputs must not be modified"
+
+
+@pytest.mark.parametrize("impl", sorted(IMPLS))
+def test_prefill_all_empty(impl):
+    x = to_dev(W.prefill_inputs([0, 0, 0], HQ=2, HV=4, seed=6))
+    out, ns = IMPLS[impl](*x.args())
+    assert out.shape == (0, 4, 128)
+    assert torch.equal(ns, x.state)
+
+
+def test_chunked_vs_recurrent_varlen_config():
+    """Config 4 shapes (8 sequences, lengths ~U[512,4096], 32 v-heads): the two independent
+    CUDA implementations agree, at a size where the CPU oracle would take minutes."""
+    lengths = W.varlen_lengths(seed=0)
+    x = W.prefill_inputs(lengths, seed=21, gen_device="cuda", device="cuda")
+    o1, s1 = prefill.kernel(*x.args())
+    o2, s2 = prefill.kernel_recurrent(*x.args())
+    assert_out_close(o1, o2, "chunked vs recurrent")
+    assert_state_close(s1, s2, PREFILL_STATE_ATOL, "chunked vs recurrent")
