@@ -124,9 +124,8 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- workloads
-def decode_workload(device, seed):
+def decode_workload(device, seed, B=256):
     from flashinfer_bench_tma_thrust_b200 import workloads as W
-    B = 256
     x = W.decode_inputs(B, seed=seed, gen_device=device, device=device)
     state_bytes = 2 * B * HV * D * D * 4
     io_bytes = (2 * B * HQ * D + B * HV * D) * 2 + B * HV * D * 2 + 2 * B * HV * 2
@@ -229,7 +228,7 @@ def run_ours(args, world, rank, local):
     result = {"n_gpus": world, "steps": K, "warmup": Wm, "higher_is_better": True,
               "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
     if args.workload == "decode":
-        x, info = decode_workload(device, seed=1000 + rank)
+        x, info = decode_workload(device, seed=1000 + rank, B=args.batch)
         B = info["B"]
         holder = {"s": x.state.clone()}
 
@@ -384,6 +383,7 @@ def main():
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill_varlen", "prefill_long"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=256, help="decode sequences per GPU")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
