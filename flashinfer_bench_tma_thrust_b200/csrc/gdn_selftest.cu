@@ -1,0 +1,104 @@
+// gdn_selftest.cu — known-answer check of the tcgen05 building blocks.
+//
+// One 128x64x128 bf16 GEMM D = A * B through shared-memory descriptors in the
+// K-major or MN-major 128B-swizzled layouts, the MMA, commit-to-mbarrier and
+// the TMEM load path that the chunked prefill kernel is built from. The GPU
+// tests compare D with a torch matmul, for all four major-ness combinations.
+#include "gdn_b200.h"
+#include "gdn_common.cuh"
+#include "sm100_umma.cuh"
+
+namespace gdn {
+namespace {
+
+using namespace sm100;
+
+// A: [128 (m)][128 (k)] row-major bf16; B: [128 (k)][64 (n)] row-major bf16; D [128][64] fp32.
+__global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16* A,
+                                                            const __nv_bfloat16* B, float* D,
+                                                            int a_mn, int b_mn, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;            // 32 KB
+  uint8_t* sB = smem + 32768;    // 16 KB
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  const int t = threadIdx.x;
+  const int warp = t >> 5;
+
+  // Fill A. K-major: 2 tiles (k halves) of 128 rows (m) x 64 cols (k).
+  //         MN-major: 2 tiles (m blocks) of 128 rows (k) x 64 cols (m).
+  for (int idx = t; idx < 128 * 128; idx += 128) {
+    const int m = idx / 128, k = idx % 128;
+    const __nv_bfloat16 val = A[idx];
+    uint32_t off;
+    if (!a_mn) off = (k / 64) * 16384 + sw128_offset(m, k % 64);
+    else off = (m / 64) * 16384 + sw128_offset(k, m % 64);
+    *reinterpret_cast<__nv_bfloat16*>(sA + off) = val;
+  }
+  // Fill B. K-major: 2 tiles (k halves) of 64 rows (n) x 64 cols (k).
+  //         MN-major: 1 tile of 128 rows (k) x 64 cols (n).
+  for (int idx = t; idx < 128 * 64; idx += 128) {
+    const int k = idx / 64, n = idx % 64;
+    const __nv_bfloat16 val = B[idx];
+    uint32_t off;
+    if (!b_mn) off = (k / 64) * 8192 + sw128_offset(n, k % 64);
+    else off = sw128_offset(k, n);
+    *reinterpret_cast<__nv_bfloat16*>(sB + off) = val;
+  }
+  if (t == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, 64);
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base;
+  if (t == 0) {
+    const uint32_t idesc = idesc_bf16(128, 64, a_mn != 0, b_mn != 0);
+    const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+    for (int s = 0; s < 8; ++s) {
+      const uint64_t ad = a_mn ? desc_mnmajor(a0 + s * 2048, 16384)
+                               : desc_kmajor(a0 + (s / 4) * 16384 + (s % 4) * 32);
+      const uint64_t bd = b_mn ? desc_mnmajor(b0 + s * 2048, 8192)
+                               : desc_kmajor(b0 + (s / 4) * 8192 + (s % 4) * 32);
+      mma_bf16(tbase, ad, bd, idesc, s > 0);
+    }
+    mma_commit(&bar);
+  }
+  const bool ok = mbar_wait(&bar, 0);
+  tc_fence_after();
+  if (!ok) {
+    if (t == 0) atomicExch(status, 1);
+  } else {
+    for (int c = 0; c < 64; c += 32) {
+      float r[32];
+      tmem_ld32(tbase + ((warp * 32u) << 16) + c, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) D[t * 64 + c + j] = r[j];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 64);
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_selftest_umma(const void* A, const void* B, float* D, int a_mn_major,
+                                 int b_mn_major, int* status, void* stream) {
+  if (!A || !B || !D || !status) return GDN_ERR_INVALID_ARG;
+  const int smem = 32768 + 16384 + 1024;
+  if (cudaFuncSetAttribute(gdn::umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem) != cudaSuccess)
+    return GDN_ERR_CUDA;
+  gdn::umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(B), D, a_mn_major,
+      b_mn_major, status);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}

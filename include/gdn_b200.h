@@ -109,6 +109,17 @@ GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* 
                               void* out, float* new_state, int64_t T, int64_t N, int32_t HQ,
                               int32_t HV, int32_t D, void* stream);
 
+/*
+ * Diagnostics. Known-answer check of the tensor-core path the chunked prefill
+ * is built on (no counterpart in the reference): D[128x64] fp32 = A[128x128] x
+ * B[128x64], bf16 row-major inputs, staged in shared memory in the K-major
+ * (0) or MN-major (1) 128B-swizzled layout and multiplied with tcgen05.mma
+ * into TMEM. *status (device int, caller zeroes it) becomes 1 if the
+ * completion wait timed out.
+ */
+GDN_API int gdn_selftest_umma(const void* A, const void* B, float* D, int a_mn_major,
+                              int b_mn_major, int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
