@@ -29,6 +29,50 @@ float resolve_scale(float scale, int32_t D) {
 
 int launch_status(int rc) { return rc == 0 ? GDN_OK : GDN_ERR_CUDA; }
 
+int fill_prefill(gdn::PrefillParams* p, const void* q, const void* k, const void* v,
+                 const float* state, const void* A_log, int A_log_dtype, const void* a,
+                 int a_dtype, const void* dt_bias, int dt_bias_dtype, const void* b, int b_dtype,
+                 const void* cu_seqlens, int cu_dtype, float scale, void* out, float* new_state,
+                 int64_t T, int64_t N, int32_t HQ, int32_t HV, int32_t D) {
+  if (T < 0 || N < 0) return GDN_ERR_INVALID_ARG;
+  int rc = check_heads(HQ, HV, D);
+  if (rc != GDN_OK) return rc;
+  if (!gate_dtype_ok(A_log_dtype) || !gate_dtype_ok(a_dtype) || !gate_dtype_ok(dt_bias_dtype) ||
+      !gate_dtype_ok(b_dtype))
+    return GDN_ERR_UNSUPPORTED_DTYPE;
+  if (cu_dtype != GDN_DTYPE_I32 && cu_dtype != GDN_DTYPE_I64) return GDN_ERR_UNSUPPORTED_DTYPE;
+  if (N == 0) return GDN_OK;
+  if (!cu_seqlens || !A_log || !dt_bias || !new_state) return GDN_ERR_INVALID_ARG;
+  if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_INVALID_ARG;
+  *p = gdn::PrefillParams{};
+  p->q = static_cast<const __nv_bfloat16*>(q);
+  p->k = static_cast<const __nv_bfloat16*>(k);
+  p->v = static_cast<const __nv_bfloat16*>(v);
+  p->state = state;
+  p->A_log = A_log;
+  p->a = a;
+  p->dt_bias = dt_bias;
+  p->b = b;
+  p->A_log_dtype = A_log_dtype;
+  p->a_dtype = a_dtype;
+  p->dt_bias_dtype = dt_bias_dtype;
+  p->b_dtype = b_dtype;
+  p->cu_seqlens = cu_seqlens;
+  p->cu_dtype = cu_dtype;
+  p->scale = resolve_scale(scale, D);
+  p->out = static_cast<__nv_bfloat16*>(out);
+  p->new_state = new_state;
+  p->T = T;
+  p->N = N;
+  p->HQ = HQ;
+  p->HV = HV;
+  return GDN_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr size_t kChunkedWorkspaceBytes = 256;  // status word (sticky error flag)
+
 }  // namespace
 
 extern "C" {
@@ -90,39 +134,50 @@ int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* v, const
                               int b_dtype, const void* cu_seqlens, int cu_dtype, float scale,
                               void* out, float* new_state, int64_t T, int64_t N, int32_t HQ,
                               int32_t HV, int32_t D, void* stream) {
-  if (T < 0 || N < 0) return GDN_ERR_INVALID_ARG;
-  int rc = check_heads(HQ, HV, D);
-  if (rc != GDN_OK) return rc;
-  if (!gate_dtype_ok(A_log_dtype) || !gate_dtype_ok(a_dtype) || !gate_dtype_ok(dt_bias_dtype) ||
-      !gate_dtype_ok(b_dtype))
-    return GDN_ERR_UNSUPPORTED_DTYPE;
-  if (cu_dtype != GDN_DTYPE_I32 && cu_dtype != GDN_DTYPE_I64) return GDN_ERR_UNSUPPORTED_DTYPE;
-  if (N == 0) return GDN_OK;
-  if (!cu_seqlens || !A_log || !dt_bias || !new_state) return GDN_ERR_INVALID_ARG;
-  if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_INVALID_ARG;
-  gdn::PrefillParams p{};
-  p.q = static_cast<const __nv_bfloat16*>(q);
-  p.k = static_cast<const __nv_bfloat16*>(k);
-  p.v = static_cast<const __nv_bfloat16*>(v);
-  p.state = state;
-  p.A_log = A_log;
-  p.a = a;
-  p.dt_bias = dt_bias;
-  p.b = b;
-  p.A_log_dtype = A_log_dtype;
-  p.a_dtype = a_dtype;
-  p.dt_bias_dtype = dt_bias_dtype;
-  p.b_dtype = b_dtype;
-  p.cu_seqlens = cu_seqlens;
-  p.cu_dtype = cu_dtype;
-  p.scale = resolve_scale(scale, D);
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.new_state = new_state;
-  p.T = T;
-  p.N = N;
-  p.HQ = HQ;
-  p.HV = HV;
+  gdn::PrefillParams p;
+  int rc = fill_prefill(&p, q, k, v, state, A_log, A_log_dtype, a, a_dtype, dt_bias,
+                        dt_bias_dtype, b, b_dtype, cu_seqlens, cu_dtype, scale, out, new_state, T,
+                        N, HQ, HV, D);
+  if (rc != GDN_OK || N == 0) return rc;
   return launch_status(gdn::launch_prefill_recurrent(p, static_cast<cudaStream_t>(stream)));
+}
+
+size_t gdn_prefill_chunked_workspace_size(int64_t T, int64_t N, int32_t HV) {
+  (void)T;
+  (void)N;
+  (void)HV;
+  return kChunkedWorkspaceBytes;
+}
+
+int gdn_prefill_chunked_fwd(const void* q, const void* k, const void* v, const float* state,
+                            const void* A_log, int A_log_dtype, const void* a, int a_dtype,
+                            const void* dt_bias, int dt_bias_dtype, const void* b, int b_dtype,
+                            const void* cu_seqlens, int cu_dtype, float scale, void* out,
+                            float* new_state, int64_t T, int64_t N, int32_t HQ, int32_t HV,
+                            int32_t D, void* workspace, size_t workspace_bytes, void* stream) {
+  gdn::PrefillParams p;
+  int rc = fill_prefill(&p, q, k, v, state, A_log, A_log_dtype, a, a_dtype, dt_bias,
+                        dt_bias_dtype, b, b_dtype, cu_seqlens, cu_dtype, scale, out, new_state, T,
+                        N, HQ, HV, D);
+  if (rc != GDN_OK || N == 0) return rc;
+  if (T > 0x7fffffffLL) return GDN_ERR_UNSUPPORTED_SHAPE;  // TMA coordinates are 32-bit
+  if (!workspace || workspace_bytes < kChunkedWorkspaceBytes) return GDN_ERR_WORKSPACE;
+  if (T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)))
+    return GDN_ERR_INVALID_ARG;
+  p.status = static_cast<int*>(workspace);
+  rc = gdn::launch_prefill_chunked(p, static_cast<cudaStream_t>(stream));
+  if (rc == -2) return GDN_ERR_CUDA;
+  return launch_status(rc);
+}
+
+int gdn_prefill_chunked_status(const void* workspace, int* host_status, void* stream) {
+  if (!workspace || !host_status) return GDN_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(host_status, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return GDN_ERR_CUDA;
+  return GDN_OK;
 }
 
 }  // extern "C"

@@ -44,9 +44,11 @@ struct PrefillParams {
   float* new_state;    // [N, HV, D, D]
   int64_t T, N;
   int HQ, HV;
+  int* status;  // chunked kernel: set to 1 if a bounded wait gave up (sticky)
 };
 
 int launch_decode(const DecodeParams& p, cudaStream_t stream);
 int launch_prefill_recurrent(const PrefillParams& p, cudaStream_t stream);
+int launch_prefill_chunked(const PrefillParams& p, cudaStream_t stream);
 
 }  // namespace gdn

@@ -100,9 +100,57 @@ def kernel_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=Non
     return run_recurrent(P, out, new_state)
 
 
+_workspaces: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device workspace of the chunked kernel (zeroed once; holds the sticky
+    status word). Grown on demand, never shrunk."""
+    key = (device.type, device.index)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def device_status(device=None) -> int:
+    """Sticky status word of the chunked kernel on `device` (0 = every bounded wait
+    completed; 1 = a wait gave up and its outputs are invalid). Synchronises."""
+    device = torch.device(device or torch.cuda.current_device())
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    ws = _workspaces.get((device.type, device.index))
+    if ws is None:
+        return 0
+    return int(ws[:4].view(torch.int32).item())
+
+
+def _aligned(t):
+    return t if t.numel() == 0 or t.data_ptr() % 16 == 0 else t.clone()
+
+
+def run_chunked(P: _Prepared, out, new_state):
+    lib = _lib.load()
+    q, k, v = _aligned(P.q), _aligned(P.k), _aligned(P.v)
+    nbytes = lib.gdn_prefill_chunked_workspace_size(P.T, P.N, P.HV)
+    ws = workspace(P.dev, nbytes)
+    with torch.cuda.device(P.dev):
+        rc = lib.gdn_prefill_chunked_fwd(
+            _ptr0(q), _ptr0(k), _ptr0(v), C.ptr(P.state),
+            P.A.data_ptr(), P.A_t, _ptr0(P.a), P.a_t, P.d.data_ptr(), P.d_t, _ptr0(P.b), P.b_t,
+            P.cu.data_ptr(), P.cu_t, P.scale, _ptr0(out), _ptr0(new_state),
+            P.T, P.N, P.HQ, P.HV, P.D, ws.data_ptr(), ws.numel(), C.stream_handle(P.dev))
+    _lib.check(rc, "gdn_prefill_chunked_fwd")
+    return out, new_state
+
+
 def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
-    """Reference-compatible prefill entry point."""
-    return kernel_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+    """Reference-compatible prefill entry point: one launch of the chunked tensor-core
+    kernel (chunk 64, state carried in fp32 in TMEM)."""
+    P = prepare(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+    out, new_state = _alloc_outputs(P)
+    return run_chunked(P, out, new_state)
 
 
 def launches_per_call() -> int:

@@ -110,6 +110,42 @@ GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* 
                               int32_t HV, int32_t D, void* stream);
 
 /*
+ * Variable-length prefill, chunked tensor-core kernel (the fast path).
+ *
+ * Replaces the solution entry kernel(q,k,v,state,A_log,a,dt_bias,b,cu_seqlens,
+ * scale) of gdn/prefill/solution/triton/kernel.py:272-347 and the reference's
+ * chunked tcgen05 prototype entry gdn/prefill/solution/cuda/chunked_proto.py:
+ * 2671-2709 (which drives a CUTLASS GEMM through ctypes from a Python loop
+ * over chunks); semantics of gdn/prefill/baseline/triton/kernel.py:18-100.
+ * Arguments as gdn_prefill_recurrent_fwd, plus:
+ *
+ *   workspace        device memory of at least
+ *                    gdn_prefill_chunked_workspace_size(T, N, HV) bytes, 16-byte
+ *                    aligned, zeroed once by the caller before its first use. It
+ *                    holds a sticky status word that the kernel sets to 1 if one of
+ *                    its bounded waits gave up (read it with
+ *                    gdn_prefill_chunked_status). Calls that share a workspace
+ *                    must be stream-ordered.
+ *
+ * q, k, v and out must be 16-byte aligned (q/k are read by TMA); T < 2^31.
+ * One launch per call; the work runs in fp32 on the state with tensor-core
+ * products carried as bf16 hi/lo pairs (about 16 significant bits).
+ */
+GDN_API size_t gdn_prefill_chunked_workspace_size(int64_t T, int64_t N, int32_t HV);
+
+GDN_API int gdn_prefill_chunked_fwd(const void* q, const void* k, const void* v,
+                                    const float* state, const void* A_log, int A_log_dtype,
+                                    const void* a, int a_dtype, const void* dt_bias,
+                                    int dt_bias_dtype, const void* b, int b_dtype,
+                                    const void* cu_seqlens, int cu_dtype, float scale, void* out,
+                                    float* new_state, int64_t T, int64_t N, int32_t HQ,
+                                    int32_t HV, int32_t D, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/* Copy the workspace status word to *host_status (synchronises `stream`). */
+GDN_API int gdn_prefill_chunked_status(const void* workspace, int* host_status, void* stream);
+
+/*
  * Diagnostics. Known-answer check of the tensor-core path the chunked prefill
  * is built on (no counterpart in the reference): D[128x64] fp32 = A[128x128] x
  * B[128x64], bf16 row-major inputs, staged in shared memory in the K-major

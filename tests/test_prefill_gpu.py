@@ -82,3 +82,11 @@ def test_chunked_vs_recurrent_varlen_config():
     o2, s2 = prefill.kernel_recurrent(*x.args())
     assert_out_close(o1, o2, "chunked vs recurrent")
     assert_state_close(s1, s2, PREFILL_STATE_ATOL, "chunked vs recurrent")
+
+
+def test_chunked_status_word_clean():
+    """Every bounded wait inside the chunked kernel completed in the calls above."""
+    x = to_dev(W.prefill_inputs([130, 7], HQ=2, HV=4, seed=31))
+    prefill.kernel(*x.args())
+    torch.cuda.synchronize()
+    assert prefill.device_status() == 0
