@@ -155,6 +155,23 @@ __device__ __forceinline__ void issue_gemm(uint32_t d, const Operand& a, const O
     for (int s = 0; s < ksteps; ++s) mma_bf16(d, op_desc(a, a.lo, s), op_desc(b, b.hi, s), idesc, 1);
 }
 
+#ifdef GDN_PHASE_PROFILE
+// Debug-only phase timer (block 0, thread 0): accumulates clock64 deltas per phase.
+__device__ long long g_phase_cycles[16];
+#define PHASE(i)                                                   \
+  do {                                                             \
+    if (blockIdx.x == 0 && threadIdx.x == 0) {                     \
+      const long long now_ = clock64();                            \
+      g_phase_cycles[i] += now_ - phase_last_;                     \
+      phase_last_ = now_;                                          \
+    }                                                              \
+  } while (0)
+#else
+#define PHASE(i) \
+  do {           \
+  } while (0)
+#endif
+
 struct ChunkTmaps {
   CUtensorMap k;  // [T, HQ, 128] bf16: dims {128, HQ, T}, box {64, 1, 64}, 128B swizzle
   CUtensorMap q;
@@ -249,6 +266,9 @@ __global__ void __launch_bounds__(128, 1)
 
   uint32_t tma_phase = 0, mma_phase = 0;
   bool ok = true;
+#ifdef GDN_PHASE_PROFILE
+  long long phase_last_ = clock64();
+#endif
   float ra = 0.f, rb = 0.f;
   issue_loads(start, end, ra, rb);
 
@@ -275,11 +295,13 @@ __global__ void __launch_bounds__(128, 1)
     cp_async_wait_all();
     __syncthreads();
 
+    PHASE(0);  // gates + scan
     // ---- wait for K/Q, then S = [K;Q] K^T and [KH;QH] = [K;Q] H ----------------------
     ok = mbar_wait(bar_tma, tma_phase);
     tma_phase ^= 1;
     sync_before_mma();
     if (!__syncthreads_and(ok)) break;
+    PHASE(1);  // TMA wait
     if (t == 0) {
       const Operand kq{smem_u32(sm + OFF_KQ), 0, false, 0, 0, 16384};
       const Operand hB{smem_u32(sm + OFF_H_HI), smem_u32(sm + OFF_H_LO), true, 8192, 2048, 0};
@@ -292,6 +314,7 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
 
+    PHASE(2);  // S, G1 MMA
     const float g_last = sG[kC - 1];
     {
       float srow[64];
@@ -359,6 +382,7 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_before();
     __syncthreads();  // sKQ, sV consumed: the next chunk's loads may start
 
+    PHASE(3);  // A/M/Kt/X build
     float nra = 0.f, nrb = 0.f;
     if (next < end) issue_loads(next, end, nra, nrb);
 
@@ -377,6 +401,7 @@ __global__ void __launch_bounds__(128, 1)
       for (int i = 0; i < 16; ++i) sTf[(b0 + i) * kSF + b0 + lane] = tc[i];
     }
     __syncthreads();
+    PHASE(4);  // diag solve
     for (int d = 1; d < 4; ++d) {
       const int nout = (4 - d) * 256;
       for (int o = t; o < nout; o += 128) {  // W_IJ = sum_{K=J}^{I-1} A_IK T_KJ  -> block (J, I)
@@ -400,6 +425,7 @@ __global__ void __launch_bounds__(128, 1)
       }
       __syncthreads();
     }
+    PHASE(5);  // off-diag solve
     {
       // T_b = T diag(beta) as the MN-major B operand: row j, cols n (half of the row per thread)
       const int j = t & (kC - 1), half = t >> 6;
@@ -428,6 +454,7 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
 
+    PHASE(6);  // T_b write
     // ---- [T_b; P] = [I; M] T_b -----------------------------------------------------
     sync_before_mma();
     if (t == 0) {
@@ -440,12 +467,14 @@ __global__ void __launch_bounds__(128, 1)
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
+    PHASE(7);  // P MMA
     {
       float r[64];
       tmem_ld64(trow + TM_S, r);
       store_row_split(sm + OFF_A2_HI, sm + OFF_A2_LO, t, r);
     }
 
+    PHASE(8);  // A2 write
     // ---- [U; O'] = [T_b; P] X ----------------------------------------------------------
     sync_before_mma();
     if (t == 0) {
@@ -458,6 +487,7 @@ __global__ void __launch_bounds__(128, 1)
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
+    PHASE(9);  // G2 MMA
     if (t < kC) {
       float u[64];
       tmem_ld64(trow + TM_2, u);
@@ -485,6 +515,7 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
 
+    PHASE(10);  // U / O
     // ---- dH = Kt^T U;  H <- gamma_last H + dH ---------------------------------------------
     sync_before_mma();
     if (t == 0) {
@@ -497,6 +528,7 @@ __global__ void __launch_bounds__(128, 1)
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
+    PHASE(11);  // G3 MMA
     {
       float dh[64];
       tmem_ld64(trow + TM_2, dh);
@@ -507,6 +539,7 @@ __global__ void __launch_bounds__(128, 1)
       tmem_st64(trow + TM_H, hrow);
       store_row_split(sm + OFF_H_HI, sm + OFF_H_LO, t, hrow);
     }
+    PHASE(12);  // H update
     ra = nra;
     rb = nrb;
   }
@@ -581,3 +614,17 @@ int launch_prefill_chunked(const PrefillParams& p, cudaStream_t stream) {
 }
 
 }  // namespace gdn
+
+#ifdef GDN_PHASE_PROFILE
+// Debug builds only: copy (and optionally reset) the per-phase cycle counters.
+extern "C" __attribute__((visibility("default"))) int gdn_debug_phase_cycles(long long* host,
+                                                                               int reset) {
+  if (cudaMemcpyFromSymbol(host, gdn::g_phase_cycles, sizeof(long long) * 16) != cudaSuccess)
+    return -1;
+  if (reset) {
+    long long z[16] = {0};
+    if (cudaMemcpyToSymbol(gdn::g_phase_cycles, z, sizeof(z)) != cudaSuccess) return -1;
+  }
+  return 0;
+}
+#endif
