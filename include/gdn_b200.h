@@ -146,6 +146,37 @@ GDN_API int gdn_prefill_chunked_fwd(const void* q, const void* k, const void* v,
 GDN_API int gdn_prefill_chunked_status(const void* workspace, int* host_status, void* stream);
 
 /*
+ * Chunked prefill that allocates nothing. No counterpart in the reference.
+ *
+ * For callers that cannot hand the library device memory: a serving engine
+ * whose memory pool owns the whole device and forbids allocations during a
+ * step (a cudaMalloc there can fail or synchronise the device), or an FFI
+ * caller without a CUDA allocator. Same arguments as gdn_prefill_chunked_fwd
+ * minus the workspace; the scratch is a 4096-byte array compiled into the
+ * library, held on every GPU that loads it until the process exits.
+ *
+ * - The first call on a device (with that device current) looks up the
+ *   array's device address once; make that first call before any stream
+ *   capture on that device.
+ * - Returns GDN_ERR_WORKSPACE if a call would need more than 4096 bytes of
+ *   scratch (the current kernel needs 256, independent of T, N and HV).
+ * - All calls share the one array, which keeps the previous call's contents;
+ *   each call zeroes the part it uses with a memset on `stream`. Calls whose
+ *   work overlaps on the GPU (different streams without ordering) race on it.
+ * - The status word is not readable from outside; outputs are valid unless a
+ *   bounded wait inside the kernel gave up.
+ * - Calls no cudaMalloc, cudaFree or other allocating routine.
+ */
+GDN_API int gdn_prefill_chunked_fwd_noalloc(const void* q, const void* k, const void* v,
+                                            const float* state, const void* A_log,
+                                            int A_log_dtype, const void* a, int a_dtype,
+                                            const void* dt_bias, int dt_bias_dtype,
+                                            const void* b, int b_dtype, const void* cu_seqlens,
+                                            int cu_dtype, float scale, void* out,
+                                            float* new_state, int64_t T, int64_t N, int32_t HQ,
+                                            int32_t HV, int32_t D, void* stream);
+
+/*
  * Diagnostics. Known-answer check of the tensor-core path the chunked prefill
  * is built on (no counterpart in the reference): D[128x64] fp32 = A[128x128] x
  * B[128x64], bf16 row-major inputs, staged in shared memory in the K-major
