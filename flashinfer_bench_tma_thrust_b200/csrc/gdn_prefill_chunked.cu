@@ -14,16 +14,18 @@
 //   X     = V - diag(gamma) KH
 //   [U; O'] = [T_b; P] X                                  (tensor cores)
 //   O     = scale (diag(gamma) QH + O')                   -> bf16 output
-//   H    <- gamma_last H + Kt^T U,  Kt_j = e^{Gamma_last-Gamma_j} k_j   (tensor cores)
+//   H    <- gamma_last H + K^T diag(f) U,  f_j = e^{Gamma_last-Gamma_j}     (tensor cores)
 //
 // One thread block (128 threads, one warpgroup) per (sequence, v-head, 64-wide
 // V tile) walks the sequence chunk by chunk. The state tile H [128 x 64] stays
 // in TMEM in fp32 for the whole sequence (TMEM lane = k). Operands that are not
-// exact bf16 (H, T_b, P, X, U, Kt) enter the bf16 tensor core as hi + lo bf16
+// exact bf16 (H, T_b, P, X, U) enter the bf16 tensor core as hi + lo bf16
 // pairs (hi*hi + hi*lo + lo*hi), which keeps about 16 significant bits; q, k and
 // v are bf16 inputs and enter exactly. K and Q chunk tiles arrive by TMA
 // (128B-swizzled, 3-D tensor maps over [token, head, dim]); the next chunk's
-// K/Q/V/gates are fetched while the current chunk's state-dependent GEMMs run.
+// tile is requested as soon as the state-update GEMM has consumed the current
+// one. Shared memory is kept under 100 KB so that two blocks run per SM and
+// each hides the other's MMA, TMA and barrier latency.
 // Padded rows of a partial chunk carry beta = 0 and log g = 0, which makes
 // their contribution to U, O and H exactly zero; their outputs are not stored.
 #include <cuda.h>
@@ -40,30 +42,38 @@ using namespace sm100;
 constexpr int kC = 64;        // chunk length
 constexpr int kVT = 64;       // V columns per thread block
 constexpr int kTiles = kHeadDim / kVT;
-constexpr int kSF = 68;       // fp32 row stride (floats) of the solve matrices
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Shared memory map (bytes from a 1024-aligned base). "hi"/"lo" pairs are the
-// two bf16 halves of a split fp32 operand.
-constexpr uint32_t OFF_KQ = 0;           // 2 x 16 KB: [k half][K rows 0..63 | Q rows 64..127], K-major
+// Shared memory map (bytes from a 1024-aligned base), 97 KB so that two blocks
+// share an SM. Regions are reused across the phases of a chunk:
+//   KQ   [k half][K rows 0..63 | Q rows 64..127], K-major, filled by TMA. The Q
+//        halves are dead once [KH; QH] is computed and then hold X (later U).
+//   H    H hi/lo (MN-major B operand of [K;Q] H). Dead between that MMA and the
+//        state update, so the fp32 solve matrices A and T live there, and T_b
+//        (hi/lo) replaces A once the solve is done.
+//   A2   [I; M] and then [T_b; P] hi/lo, K-major rows m (128) x cols j.
+constexpr uint32_t OFF_KQ = 0;           // 32 KB
+constexpr uint32_t OFF_X_HI = 8192;      // 8 KB (Q half 0): X then diag(f) U, MN-major rows j x cols v
+constexpr uint32_t OFF_X_LO = 24576;     // 8 KB (Q half 1)
 constexpr uint32_t OFF_H_HI = 32768;     // 16 KB: H, MN-major: rows k (128) x cols v (64)
 constexpr uint32_t OFF_H_LO = 49152;
-constexpr uint32_t OFF_X_HI = 65536;     // 8 KB: X then U, MN-major: rows j (64) x cols v (64)
-constexpr uint32_t OFF_X_LO = 73728;
-constexpr uint32_t OFF_A2_HI = 81920;    // 16 KB: [I; M] then [T_b; P], K-major: rows m (128) x cols j
-constexpr uint32_t OFF_A2_LO = 98304;
-constexpr uint32_t OFF_KT_HI = 114688;   // 16 KB: Kt, MN-major: 2 blocks (k halves) x rows j x cols k
-constexpr uint32_t OFF_KT_LO = 131072;
-constexpr uint32_t OFF_TB_HI = 147456;   // 8 KB: T_b, MN-major: rows j x cols n
-constexpr uint32_t OFF_TB_LO = 155648;
-constexpr uint32_t OFF_V = 163840;       // 8 KB: V tile, rows j x 64 bf16 (16-byte chunks swizzled)
-constexpr uint32_t OFF_AF = 172032;      // 64 x 68 fp32: A
-constexpr uint32_t OFF_TF = 189440;      // 64 x 68 fp32: T (upper blocks: scratch)
-constexpr uint32_t OFF_G = 206848;       // 64 fp32: Gamma * log2(e)
-constexpr uint32_t OFF_BETA = 207104;    // 64 fp32: beta
-constexpr uint32_t OFF_BAR = 207360;     // 2 mbarriers + TMEM base
-constexpr uint32_t kSmemUsed = 207424;
+constexpr uint32_t OFF_AF = 32768;       // 64 x 64 fp32 A (swizzled columns), aliases H hi
+constexpr uint32_t OFF_TF = 49152;       // 64 x 64 fp32 T (upper blocks: scratch), aliases H lo
+constexpr uint32_t OFF_TB_HI = 32768;    // 8 KB: T_b, MN-major rows j x cols n (after the solve)
+constexpr uint32_t OFF_TB_LO = 40960;
+constexpr uint32_t OFF_A2_HI = 65536;    // 16 KB
+constexpr uint32_t OFF_A2_LO = 81920;
+constexpr uint32_t OFF_G = 98304;        // 64 fp32: Gamma * log2(e)
+constexpr uint32_t OFF_BETA = 98560;     // 64 fp32: beta
+constexpr uint32_t OFF_BAR = 98816;      // 2 mbarriers + TMEM base
+constexpr uint32_t kSmemUsed = 98880;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + alignment slack
+
+// fp32 64 x 64 matrices with the 16-byte column groups XOR-swizzled by row, so
+// that row-per-thread float4 writes and column reads are free of bank conflicts.
+__device__ __forceinline__ int fidx(int r, int c) {
+  return r * 64 + ((((c >> 2) ^ r) & 15) << 2) + (c & 3);
+}
 
 // TMEM columns (fp32, lane = row of M = 128)
 constexpr uint32_t kTmemCols = 256;
@@ -177,12 +187,12 @@ struct ChunkTmaps {
   CUtensorMap q;
 };
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, 2)
     prefill_chunked_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  float* sAf = reinterpret_cast<float*>(sm + OFF_AF);
+  float* sAf = reinterpret_cast<float*>(sm + OFF_AF);  // (aliases H hi, see the map)
   float* sTf = reinterpret_cast<float*>(sm + OFF_TF);
   float* sG = reinterpret_cast<float*>(sm + OFF_G);
   float* sBeta = reinterpret_cast<float*>(sm + OFF_BETA);
@@ -239,11 +249,10 @@ __global__ void __launch_bounds__(128, 1)
   const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
   const int64_t HV = p.HV;
 
-  // chunk loader: TMA for K/Q (thread 0), cp.async for the V tile and plain loads
-  // of the raw gates (threads 0..63, one token each)
-  auto issue_loads = [&](int64_t cs, int64_t ce, float& ra, float& rb) {
+  // K/Q tiles by TMA (thread 0); raw gates of the chunk's tokens (threads 0..63)
+  auto issue_tma = [&](int64_t cs) {
     if (t == 0) {
-      fence_async_smem();  // order earlier generic reads of the K/Q tile before the TMA writes
+      fence_async_smem();  // order earlier generic accesses of the tile before the TMA writes
       mbar_arrive_expect_tx(bar_tma, 4 * 8192);
       const int tok = static_cast<int>(cs);
       tma_load_3d(sm + OFF_KQ, &maps.k, bar_tma, 0, qh, tok);
@@ -251,14 +260,11 @@ __global__ void __launch_bounds__(128, 1)
       tma_load_3d(sm + OFF_KQ + 16384, &maps.k, bar_tma, 64, qh, tok);
       tma_load_3d(sm + OFF_KQ + 16384 + 8192, &maps.q, bar_tma, 64, qh, tok);
     }
+  };
+  auto load_gates = [&](int64_t cs, int64_t ce, float& ra, float& rb) {
     if (t < kC) {
       const int64_t tok = cs + t;
       const bool valid = tok < ce;
-      const __nv_bfloat16* src = p.v + ((valid ? tok : cs) * HV + h) * kHeadDim + vt * kVT;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        cp_async16(sm + OFF_V + sw128_chunk(t, c), src + c * 8, valid ? 16u : 0u);
-      cp_async_commit();
       ra = valid ? load_scalar(p.a, p.a_dtype, tok * HV + h) : 0.0f;
       rb = valid ? load_scalar(p.b, p.b_dtype, tok * HV + h) : 0.0f;
     }
@@ -270,7 +276,8 @@ __global__ void __launch_bounds__(128, 1)
   long long phase_last_ = clock64();
 #endif
   float ra = 0.f, rb = 0.f;
-  issue_loads(start, end, ra, rb);
+  issue_tma(start);
+  load_gates(start, end, ra, rb);
 
   for (int64_t cs = start; cs < end; cs += kC) {
     const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
@@ -292,7 +299,6 @@ __global__ void __launch_bounds__(128, 1)
     }
     __syncthreads();
     if (t >= 32 && t < kC) sG[t] += sG[31];
-    cp_async_wait_all();
     __syncthreads();
 
     PHASE(0);  // gates + scan
@@ -309,6 +315,19 @@ __global__ void __launch_bounds__(128, 1)
       issue_gemm(tmem + TM_1, kq, hB, ID_KM, 8);
       mma_commit(bar_mma);
     }
+    // V row of this thread's token (independent of the MMAs; latency overlaps them)
+    uint4 vraw[8];
+    if (t < kC) {
+      if (t < L) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.v + ((cs + t) * HV + h) * kHeadDim + vt * kVT);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) vraw[c] = src[c];
+      } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) vraw[c] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
     ok = mbar_wait(bar_mma, mma_phase);
     mma_phase ^= 1;
     tc_fence_after();
@@ -322,7 +341,6 @@ __global__ void __launch_bounds__(128, 1)
       if (t < kC) {
         // A row i = t (fp32, for the solve); identity row of [I; M]
         const float gi = sG[t], bi = sBeta[t];
-        float* arow = sAf + t * kSF;
 #pragma unroll
         for (int j = 0; j < kC; j += 4) {
           float4 w;
@@ -330,7 +348,7 @@ __global__ void __launch_bounds__(128, 1)
           w.y = (j + 1 < t) ? bi * ex2(gi - sG[j + 1]) * srow[j + 1] : 0.f;
           w.z = (j + 2 < t) ? bi * ex2(gi - sG[j + 2]) * srow[j + 2] : 0.f;
           w.w = (j + 3 < t) ? bi * ex2(gi - sG[j + 3]) * srow[j + 3] : 0.f;
-          *reinterpret_cast<float4*>(arow + j) = w;
+          *reinterpret_cast<float4*>(sAf + fidx(t, j)) = w;
         }
 #pragma unroll
         for (int j = 0; j < kC; ++j) srow[j] = (j == t) ? 1.0f : 0.0f;
@@ -344,33 +362,14 @@ __global__ void __launch_bounds__(128, 1)
         store_row_split(sm + OFF_A2_HI, sm + OFF_A2_LO, t, srow);
       }
     }
-    {
-      // Kt row j = t & 63, k half = t >> 6:  Kt_j = e^{Gamma_last - Gamma_j} k_j (0 if padded)
-      const int j = t & (kC - 1), kh = t >> 6;
-      const float f = (j < L) ? ex2(g_last - sG[j]) : 0.0f;
-      float kv[64];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 raw =
-            *reinterpret_cast<const uint4*>(sm + OFF_KQ + kh * 16384 + sw128_chunk(j, c));
-        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          kv[c * 8 + 2 * e] = f * __uint_as_float(w[e] << 16);
-          kv[c * 8 + 2 * e + 1] = f * __uint_as_float(w[e] & 0xffff0000u);
-        }
-      }
-      store_row_split(sm + OFF_KT_HI + kh * 8192, sm + OFF_KT_LO + kh * 8192, j, kv);
-    }
     if (t < kC) {
-      // X row j = t:  V_j - gamma_j (K H)_j
+      // X row j = t:  V_j - gamma_j (K H)_j, into the dead Q half of the tile
       float xr[64];
       tmem_ld64(trow + TM_1, xr);
       const float gam = ex2(sG[t]);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(sm + OFF_V + sw128_chunk(t, c));
-        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        const uint32_t w[4] = {vraw[c].x, vraw[c].y, vraw[c].z, vraw[c].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           xr[c * 8 + 2 * e] = __uint_as_float(w[e] << 16) - gam * xr[c * 8 + 2 * e];
@@ -379,12 +378,11 @@ __global__ void __launch_bounds__(128, 1)
       }
       store_row_split(sm + OFF_X_HI, sm + OFF_X_LO, t, xr);
     }
-    tc_fence_before();
-    __syncthreads();  // sKQ, sV consumed: the next chunk's loads may start
+    __syncthreads();
 
-    PHASE(3);  // A/M/Kt/X build
+    PHASE(3);  // A/M/X build
     float nra = 0.f, nrb = 0.f;
-    if (next < end) issue_loads(next, end, nra, nrb);
+    if (next < end) load_gates(next, end, nra, nrb);
 
     // ---- T = (I + A)^-1, blocked 16 x 16 ---------------------------------------------
     if (lane < 16) {
@@ -394,49 +392,75 @@ __global__ void __launch_bounds__(128, 1)
       for (int i = 0; i < 16; ++i) {
         float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < i; ++j) s = fmaf(sAf[(b0 + i) * kSF + b0 + j], tc[j], s);
+        for (int j = 0; j < i; ++j) s = fmaf(sAf[fidx(b0 + i, b0 + j)], tc[j], s);
         tc[i] = (i < lane) ? 0.f : ((i == lane) ? 1.f : -s);
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) sTf[(b0 + i) * kSF + b0 + lane] = tc[i];
+      for (int i = 0; i < 16; ++i) sTf[fidx(b0 + i, b0 + lane)] = tc[i];
     }
     __syncthreads();
     PHASE(4);  // diag solve
-    for (int d = 1; d < 4; ++d) {
-      const int nout = (4 - d) * 256;
-      for (int o = t; o < nout; o += 128) {  // W_IJ = sum_{K=J}^{I-1} A_IK T_KJ  -> block (J, I)
-        const int I = d + o / 256, J = I - d, r = (o & 255) >> 4, c = o & 15;
-        float s = 0.f;
-        for (int K = J; K < I; ++K) {
+    // Off-diagonal blocks by distance d = I - J: one warp per block, each lane
+    // owns row r = lane/2 and 8 columns c0 = 8*(lane&1) of the 16 x 16 block.
+    {
+      const int r = lane >> 1, c0 = (lane & 1) * 8;
+      for (int d = 1; d < 4; ++d) {
+        const int I = d + warp, J = warp;
+        float w[8];
+        if (warp < 4 - d) {  // W_IJ = sum_{K=J}^{I-1} A_IK T_KJ  -> scratch block (J, I)
 #pragma unroll
-          for (int k = 0; k < 16; ++k)
-            s = fmaf(sAf[(16 * I + r) * kSF + 16 * K + k], sTf[(16 * K + k) * kSF + 16 * J + c], s);
+          for (int e = 0; e < 8; ++e) w[e] = 0.f;
+          for (int K = J; K < I; ++K) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const float a = sAf[fidx(16 * I + r, 16 * K + k)];
+              const float4 t0 = *reinterpret_cast<const float4*>(sTf + fidx(16 * K + k, 16 * J + c0));
+              const float4 t1 = *reinterpret_cast<const float4*>(sTf + fidx(16 * K + k, 16 * J + c0 + 4));
+              w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
+              w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
+              w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
+              w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
+            }
+          }
+          *reinterpret_cast<float4*>(sTf + fidx(16 * J + r, 16 * I + c0)) =
+              make_float4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<float4*>(sTf + fidx(16 * J + r, 16 * I + c0 + 4)) =
+              make_float4(w[4], w[5], w[6], w[7]);
         }
-        sTf[(16 * J + r) * kSF + 16 * I + c] = s;
-      }
-      __syncthreads();
-      for (int o = t; o < nout; o += 128) {  // T_IJ = -T_II W_IJ
-        const int I = d + o / 256, J = I - d, r = (o & 255) >> 4, c = o & 15;
-        float s = 0.f;
+        __syncwarp();
+        if (warp < 4 - d) {  // T_IJ = -T_II W_IJ (W read back from the scratch block)
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-          s = fmaf(sTf[(16 * I + r) * kSF + 16 * I + k], sTf[(16 * J + k) * kSF + 16 * I + c], s);
-        sTf[(16 * I + r) * kSF + 16 * J + c] = -s;
+          for (int e = 0; e < 8; ++e) w[e] = 0.f;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float a = sTf[fidx(16 * I + r, 16 * I + k)];
+            const float4 t0 = *reinterpret_cast<const float4*>(sTf + fidx(16 * J + k, 16 * I + c0));
+            const float4 t1 = *reinterpret_cast<const float4*>(sTf + fidx(16 * J + k, 16 * I + c0 + 4));
+            w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
+            w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
+            w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
+            w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
+          }
+          *reinterpret_cast<float4*>(sTf + fidx(16 * I + r, 16 * J + c0)) =
+              make_float4(-w[0], -w[1], -w[2], -w[3]);
+          *reinterpret_cast<float4*>(sTf + fidx(16 * I + r, 16 * J + c0 + 4)) =
+              make_float4(-w[4], -w[5], -w[6], -w[7]);
+        }
+        __syncthreads();
       }
-      __syncthreads();
     }
     PHASE(5);  // off-diag solve
     {
-      // T_b = T diag(beta) as the MN-major B operand: row j, cols n (half of the row per thread)
+      // T_b = T diag(beta) as the MN-major B operand: row j, cols n (half of the row per
+      // thread); written over A, which the solve no longer needs
       const int j = t & (kC - 1), half = t >> 6;
       float vals[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
         const int nn = half * 32 + c;
         const bool lower = (nn >> 4) < (j >> 4) || ((nn >> 4) == (j >> 4) && nn <= j);
-        vals[c] = lower ? sTf[j * kSF + nn] * sBeta[nn] : 0.f;
+        vals[c] = lower ? sTf[fidx(j, nn)] * sBeta[nn] : 0.f;
       }
-      // this thread writes chunks 4*half .. 4*half+3 of row j
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t hw[4], lw[4];
@@ -489,9 +513,14 @@ __global__ void __launch_bounds__(128, 1)
     if (!__syncthreads_and(ok)) break;
     PHASE(9);  // G2 MMA
     if (t < kC) {
+      // f_j U_j with f_j = e^{Gamma_last - Gamma_j} (0 for padded rows): the state
+      // update then reads the raw K tile, dH = K^T diag(f) U
       float u[64];
       tmem_ld64(trow + TM_2, u);
-      store_row_split(sm + OFF_X_HI, sm + OFF_X_LO, t, u);  // U overwrites X (G2 is done)
+      const float f = (t < L) ? ex2(g_last - sG[t]) : 0.0f;
+#pragma unroll
+      for (int v = 0; v < kVT; ++v) u[v] *= f;
+      store_row_split(sm + OFF_X_HI, sm + OFF_X_LO, t, u);  // overwrites X (G2 is done)
     } else {
       const int i = t - kC;
       float o[64], qhv[64];
@@ -516,10 +545,10 @@ __global__ void __launch_bounds__(128, 1)
     }
 
     PHASE(10);  // U / O
-    // ---- dH = Kt^T U;  H <- gamma_last H + dH ---------------------------------------------
+    // ---- dH = K^T diag(f) U;  H <- gamma_last H + dH ----------------------------------------
     sync_before_mma();
     if (t == 0) {
-      const Operand kt{smem_u32(sm + OFF_KT_HI), smem_u32(sm + OFF_KT_LO), true, 8192, 2048, 0};
+      const Operand kt{smem_u32(sm + OFF_KQ), 0, true, 16384, 2048, 0};
       const Operand ub{smem_u32(sm + OFF_X_HI), smem_u32(sm + OFF_X_LO), true, 8192, 2048, 0};
       issue_gemm(tmem + TM_2, kt, ub, ID_MM, 4);
       mma_commit(bar_mma);
@@ -528,6 +557,8 @@ __global__ void __launch_bounds__(128, 1)
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
+    // the K/Q tile is free: fetch the next chunk while the state is updated
+    if (next < end) issue_tma(next);
     PHASE(11);  // G3 MMA
     {
       float dh[64];
