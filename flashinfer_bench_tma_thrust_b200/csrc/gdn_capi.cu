@@ -71,7 +71,7 @@ int fill_prefill(gdn::PrefillParams* p, const void* q, const void* k, const void
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-constexpr size_t kChunkedWorkspaceBytes = 256;  // status word (sticky error flag)
+constexpr size_t kChunkedWorkspaceBytes = 256;  // fused path: status word (sticky error flag)
 
 }  // namespace
 
@@ -143,10 +143,9 @@ int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* v, const
 }
 
 size_t gdn_prefill_chunked_workspace_size(int64_t T, int64_t N, int32_t HV) {
-  (void)T;
-  (void)N;
-  (void)HV;
-  return kChunkedWorkspaceBytes;
+  if (T < 0 || N < 0 || HV <= 0) return kChunkedWorkspaceBytes;
+  const size_t two = gdn::prefill_twophase_workspace_bytes(T, N, HV);
+  return two > kChunkedWorkspaceBytes ? two : kChunkedWorkspaceBytes;
 }
 
 int gdn_prefill_chunked_fwd(const void* q, const void* k, const void* v, const float* state,
@@ -165,7 +164,12 @@ int gdn_prefill_chunked_fwd(const void* q, const void* k, const void* v, const f
   if (T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)))
     return GDN_ERR_INVALID_ARG;
   p.status = static_cast<int*>(workspace);
-  rc = gdn::launch_prefill_chunked(p, static_cast<cudaStream_t>(stream));
+  // two-phase (parallel prep + state scan) when the workspace holds the per-chunk
+  // [T_b; P] images, otherwise the fused single-kernel path (256 bytes)
+  if (workspace_bytes >= gdn::prefill_twophase_workspace_bytes(T, N, HV))
+    rc = gdn::launch_prefill_twophase(p, workspace, static_cast<cudaStream_t>(stream));
+  else
+    rc = gdn::launch_prefill_chunked(p, static_cast<cudaStream_t>(stream));
   if (rc == -2) return GDN_ERR_CUDA;
   return launch_status(rc);
 }

@@ -50,5 +50,7 @@ struct PrefillParams {
 int launch_decode(const DecodeParams& p, cudaStream_t stream);
 int launch_prefill_recurrent(const PrefillParams& p, cudaStream_t stream);
 int launch_prefill_chunked(const PrefillParams& p, cudaStream_t stream);
+size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV);
+int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_t stream);
 
 }  // namespace gdn

@@ -17,6 +17,7 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 4096;  // stated maximum scratch for one call
+constexpr size_t kFusedScratchBytes = 256;     // what the fused single-kernel path needs
 constexpr int kMaxDevices = 64;
 
 // The scratch itself. In host code this name is only a stand-in for the device
@@ -48,7 +49,9 @@ extern "C" int gdn_prefill_chunked_fwd_noalloc(
     int A_log_dtype, const void* a, int a_dtype, const void* dt_bias, int dt_bias_dtype,
     const void* b, int b_dtype, const void* cu_seqlens, int cu_dtype, float scale, void* out,
     float* new_state, int64_t T, int64_t N, int32_t HQ, int32_t HV, int32_t D, void* stream) {
-  const size_t need = gdn_prefill_chunked_workspace_size(T, N, HV);
+  // Given less workspace than its two-phase path needs, gdn_prefill_chunked_fwd runs
+  // the fused single-kernel path, whose scratch is the 256-byte status word.
+  const size_t need = kFusedScratchBytes;
   if (need > kNoAllocScratchBytes) return GDN_ERR_WORKSPACE;
   void* scratch = nullptr;
   const int rc = scratch_for_current_device(&scratch);

@@ -1,0 +1,501 @@
+// gdn_prefill_twophase.cu — chunk-64 varlen GDN prefill split into a parallel
+// prep phase and a sequential scan phase (the default prefill path).
+//
+// Same algebra as gdn_prefill_chunked.cu (chunkwise / UT-transform gated delta
+// rule; semantics of gdn/prefill/baseline/triton/kernel.py:18-100). The work of
+// a chunk splits into a part that does not depend on the state and a part that
+// does:
+//
+//   prep (one block per (chunk, v-head), all chunks of all sequences at once):
+//     S = [K;Q] K^T, A, M, T_b = (I + A)^-1 diag(beta), [T_b; P] = [I; M] T_b
+//     -> the bf16 image of [T_b; P] (hi 128 rows, lo rows 0..63: 24 KB) written to
+//        the workspace in the 128B-swizzled layout the scan kernel's MMA reads.
+//   scan (one block per (sequence, v-head, 64-wide V tile), chunk by chunk):
+//     [KH; QH] = [K;Q] H,  X = V - gamma KH,  [U; O'] = [T_b; P] X,
+//     O = scale (gamma QH + O'),  H <- gamma_last H + K^T diag(f) U.
+//
+// The prep phase has (T/64 + N) x HV independent blocks, so the triangular solve
+// and the operand construction run at full occupancy instead of on the critical
+// path of each sequence; the scan keeps only the state chain and receives
+// [T_b; P] with one bulk copy per chunk. P enters the tensor core as hi only (its
+// rounding only touches the output, which is bf16), T_b as hi + lo.
+// A tiny first kernel turns cu_seqlens into per-sequence chunk offsets so that
+// no host synchronisation is needed.
+#include "gdn_chunk_common.cuh"
+#include "gdn_launch.h"
+
+namespace gdn {
+namespace {
+
+using namespace sm100;
+using namespace chunk;
+
+constexpr uint32_t kA2Bytes = 24576;  // per (chunk, v-head): hi 16 KB + lo rows 0..63 8 KB
+
+__device__ __forceinline__ void seq_bounds(const PrefillParams& p, int64_t n, int64_t& start,
+                                           int64_t& end) {
+  start = load_index(p.cu_seqlens, p.cu_dtype, n);
+  end = load_index(p.cu_seqlens, p.cu_dtype, n + 1);
+  start = start < 0 ? 0 : (start > p.T ? p.T : start);
+  end = end < 0 ? 0 : (end > p.T ? p.T : end);
+}
+
+// ------------------------------------------------------------------ chunk offsets
+// offs[n] = number of 64-token chunks in sequences 0..n-1 (offs[0] = 0). One block.
+__global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams p,
+                                                             int64_t* offs) {
+  __shared__ int64_t warp_sums[32];
+  __shared__ int64_t carry;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  if (t == 0) {
+    carry = 0;
+    offs[0] = 0;
+  }
+  __syncthreads();
+  for (int64_t base = 0; base < p.N; base += 1024) {
+    const int64_t n = base + t;
+    int64_t cnt = 0;
+    if (n < p.N) {
+      int64_t s, e;
+      seq_bounds(p, n, s, e);
+      cnt = e > s ? (e - s + kC - 1) / kC : 0;
+    }
+    int64_t x = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int64_t w = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sums[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int64_t incl = x + (warp > 0 ? warp_sums[warp - 1] : 0) + carry;
+    if (n < p.N) offs[n + 1] = incl;
+    __syncthreads();
+    if (t == 1023) carry = incl;
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ prep
+// Shared memory: KQ tile (32 KB, TMA) — dead after S, then the fp32 A (0..16 KB)
+// and T (16..32 KB) of the solve, then T_b hi/lo over A; [I; M] hi/lo (32 KB).
+constexpr uint32_t P_OFF_KQ = 0;
+constexpr uint32_t P_OFF_AF = 0;
+constexpr uint32_t P_OFF_TF = 16384;
+constexpr uint32_t P_OFF_TB_HI = 0;
+constexpr uint32_t P_OFF_TB_LO = 8192;
+constexpr uint32_t P_OFF_A2_HI = 32768;
+constexpr uint32_t P_OFF_A2_LO = 49152;
+constexpr uint32_t P_OFF_G = 65536;
+constexpr uint32_t P_OFF_BETA = 65792;
+constexpr uint32_t P_OFF_BAR = 66048;
+constexpr uint32_t kPrepSmem = 66112 + 1024;
+constexpr uint32_t kPrepTmemCols = 128;
+constexpr uint32_t PT_S = 0, PT_P = 64;
+
+__global__ void __launch_bounds__(128, 3)
+    prep_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
+                const int64_t* __restrict__ offs, uint8_t* __restrict__ a2_out) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~uintptr_t(1023));
+  float* sAf = reinterpret_cast<float*>(sm + P_OFF_AF);
+  float* sTf = reinterpret_cast<float*>(sm + P_OFF_TF);
+  float* sG = reinterpret_cast<float*>(sm + P_OFF_G);
+  float* sBeta = reinterpret_cast<float*>(sm + P_OFF_BETA);
+  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(sm + P_OFF_BAR);
+  uint64_t* bar_mma = bar_tma + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P_OFF_BAR + 16);
+
+  const int t = threadIdx.x, warp = t >> 5;
+  const int h = static_cast<int>(blockIdx.x % p.HV);
+  const int64_t gchunk = blockIdx.x / p.HV;
+  const int64_t total = offs[p.N];
+  if (gchunk >= total) return;
+  // sequence containing this chunk: the last n with offs[n] <= gchunk
+  int64_t lo = 0, hi = p.N;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (offs[mid] <= gchunk) lo = mid;
+    else hi = mid - 1;
+  }
+  const int64_t n = lo;
+  int64_t start, end;
+  seq_bounds(p, n, start, end);
+  const int64_t cs = start + (gchunk - offs[n]) * kC;
+  const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
+  const int qh = h / (p.HV / p.HQ);
+
+  if (t == 0) {
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(bar_tma, 4 * 8192);
+    const int tok = static_cast<int>(cs);
+    tma_load_3d(sm + P_OFF_KQ, &maps.k, bar_tma, 0, qh, tok);
+    tma_load_3d(sm + P_OFF_KQ + 8192, &maps.q, bar_tma, 0, qh, tok);
+    tma_load_3d(sm + P_OFF_KQ + 16384, &maps.k, bar_tma, 64, qh, tok);
+    tma_load_3d(sm + P_OFF_KQ + 16384 + 8192, &maps.q, bar_tma, 64, qh, tok);
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, kPrepTmemCols);
+  float ra = 0.f, rb = 0.f;
+  if (t < kC && t < L) {
+    ra = load_scalar(p.a, p.a_dtype, (cs + t) * p.HV + h);
+    rb = load_scalar(p.b, p.b_dtype, (cs + t) * p.HV + h);
+  }
+  const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
+  const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+
+  chunk_gates(ra, rb, L, A_log, dtb, sG, sBeta);
+  bool ok = mbar_wait(bar_tma, 0);
+  sync_before_mma();
+  if (__syncthreads_and(ok)) {
+    if (t == 0) {
+      const Operand kq{smem_u32(sm + P_OFF_KQ), 0, false, 0, 0, 16384};
+      issue_gemm(tmem + PT_S, kq, kq, ID_KK, 8);
+      mma_commit(bar_mma);
+    }
+    ok = mbar_wait(bar_mma, 0);
+    tc_fence_after();
+    if (__syncthreads_and(ok)) {
+      // the K/Q tile is dead: A, T and T_b reuse its space
+      build_a_m(trow + PT_S, sAf, sG, sBeta, sm + P_OFF_A2_HI, sm + P_OFF_A2_LO);
+      __syncthreads();
+      solve_tb(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
+      sync_before_mma();
+      if (t == 0) {
+        const Operand a2{smem_u32(sm + P_OFF_A2_HI), smem_u32(sm + P_OFF_A2_LO), false, 0, 0, 0};
+        const Operand tb{smem_u32(sm + P_OFF_TB_HI), smem_u32(sm + P_OFF_TB_LO), true, 8192,
+                         2048, 0};
+        issue_gemm(tmem + PT_P, a2, tb, ID_KM, 4);
+        mma_commit(bar_mma);
+      }
+      ok = mbar_wait(bar_mma, 1);
+      tc_fence_after();
+      if (__syncthreads_and(ok)) {
+        // row t of [T_b; P] -> hi (all rows) and lo (rows 0..63) swizzled image in HBM
+        float r[64];
+        tmem_ld64(trow + PT_P, r);
+        uint8_t* dst = a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) * kA2Bytes;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat16 h0, l0, h1, l1;
+            split_bf16(r[c * 8 + 2 * e], h0, l0);
+            split_bf16(r[c * 8 + 2 * e + 1], h1, l1);
+            hw[e] = pack_bf16(h0, h1);
+            lw[e] = pack_bf16(l0, l1);
+          }
+          const uint32_t off = sw128_chunk(t, c);
+          *reinterpret_cast<uint4*>(dst + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          if (t < kC)
+            *reinterpret_cast<uint4*>(dst + 16384 + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      }
+    }
+  }
+  if (!ok && t == 0 && p.status) atomicExch(p.status, 1);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kPrepTmemCols);
+}
+
+// ------------------------------------------------------------------ scan
+// Shared memory: KQ tile (32 KB; its Q halves hold X and then diag(f) U),
+// H hi/lo (32 KB), [T_b; P] hi/lo (32 KB; lo rows 64..127 stay zero).
+constexpr uint32_t S_OFF_KQ = 0;
+constexpr uint32_t S_OFF_X_HI = 8192;
+constexpr uint32_t S_OFF_X_LO = 24576;
+constexpr uint32_t S_OFF_H_HI = 32768;
+constexpr uint32_t S_OFF_H_LO = 49152;
+constexpr uint32_t S_OFF_A2_HI = 65536;
+constexpr uint32_t S_OFF_A2_LO = 81920;
+constexpr uint32_t S_OFF_G = 98304;
+constexpr uint32_t S_OFF_BETA = 98560;
+constexpr uint32_t S_OFF_BAR = 98816;
+constexpr uint32_t kScanSmem = 98880 + 1024;
+constexpr uint32_t kScanTmemCols = 256;
+constexpr uint32_t ST_H = 0, ST_1 = 64, ST_2 = 128;
+
+__global__ void __launch_bounds__(128, 2)
+    scan_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
+                const int64_t* __restrict__ offs, const uint8_t* __restrict__ a2_in) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~uintptr_t(1023));
+  float* sG = reinterpret_cast<float*>(sm + S_OFF_G);
+  float* sBeta = reinterpret_cast<float*>(sm + S_OFF_BETA);
+  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(sm + S_OFF_BAR);
+  uint64_t* bar_a2 = bar_tma + 1;
+  uint64_t* bar_mma = bar_tma + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S_OFF_BAR + 32);
+
+  const int t = threadIdx.x, warp = t >> 5;
+  const int64_t unit = blockIdx.x;
+  const int vt = static_cast<int>(unit % kTiles);
+  const int h = static_cast<int>((unit / kTiles) % p.HV);
+  const int64_t n = unit / (kTiles * p.HV);
+  const int qh = h / (p.HV / p.HQ);
+  const int64_t HV = p.HV;
+  int64_t start, end;
+  seq_bounds(p, n, start, end);
+
+  const int64_t sbase = ((n * p.HV + h) * kHeadDim + vt * kVT) * kHeadDim + t;
+  float hrow[kVT];
+#pragma unroll
+  for (int v = 0; v < kVT; ++v) hrow[v] = p.state ? p.state[sbase + v * kHeadDim] : 0.0f;
+  if (end <= start) {  // empty sequence: pass the state through
+#pragma unroll
+    for (int v = 0; v < kVT; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
+    return;
+  }
+  const uint8_t* a2_seq = a2_in + static_cast<uint64_t>(offs[n]) * HV * kA2Bytes +
+                          static_cast<uint64_t>(h) * kA2Bytes;
+  const uint64_t a2_chunk_stride = static_cast<uint64_t>(HV) * kA2Bytes;
+
+  auto issue_tma = [&](int64_t cs) {
+    fence_async_smem();
+    mbar_arrive_expect_tx(bar_tma, 4 * 8192);
+    const int tok = static_cast<int>(cs);
+    tma_load_3d(sm + S_OFF_KQ, &maps.k, bar_tma, 0, qh, tok);
+    tma_load_3d(sm + S_OFF_KQ + 8192, &maps.q, bar_tma, 0, qh, tok);
+    tma_load_3d(sm + S_OFF_KQ + 16384, &maps.k, bar_tma, 64, qh, tok);
+    tma_load_3d(sm + S_OFF_KQ + 16384 + 8192, &maps.q, bar_tma, 64, qh, tok);
+  };
+  auto issue_a2 = [&](int64_t c) {
+    fence_async_smem();
+    mbar_arrive_expect_tx(bar_a2, kA2Bytes);
+    const uint8_t* src = a2_seq + static_cast<uint64_t>(c) * a2_chunk_stride;
+    bulk_load(sm + S_OFF_A2_HI, src, 16384, bar_a2);
+    bulk_load(sm + S_OFF_A2_LO, src + 16384, 8192, bar_a2);
+  };
+
+  if (t == 0) {
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_a2, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, kScanTmemCols);
+  // the lo half of [T_b; P] has no P rows: rows 64..127 stay zero
+  for (int i = t; i < 8192 / 16; i += 128)
+    reinterpret_cast<uint4*>(sm + S_OFF_A2_LO + 8192)[i] = make_uint4(0u, 0u, 0u, 0u);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  tmem_st64(trow + ST_H, hrow);
+  store_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, t, hrow);
+
+  const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
+  const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
+  auto load_gates = [&](int64_t cs, float& ra, float& rb) {
+    if (t < kC) {
+      const int64_t tok = cs + t;
+      const bool valid = tok < end;
+      ra = valid ? load_scalar(p.a, p.a_dtype, tok * HV + h) : 0.0f;
+      rb = valid ? load_scalar(p.b, p.b_dtype, tok * HV + h) : 0.0f;
+    }
+  };
+
+  uint32_t tma_phase = 0, a2_phase = 0, mma_phase = 0;
+  bool ok = true;
+  float ra = 0.f, rb = 0.f;
+  if (t == 0) {
+    issue_tma(start);
+    issue_a2(0);
+  }
+  load_gates(start, ra, rb);
+
+  int64_t c = 0;
+  for (int64_t cs = start; cs < end; cs += kC, ++c) {
+    const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
+    const int64_t next = cs + kC;
+    chunk_gates(ra, rb, L, A_log, dtb, sG, sBeta);
+
+    // ---- [KH; QH] = [K;Q] H --------------------------------------------------------
+    ok = mbar_wait(bar_tma, tma_phase);
+    tma_phase ^= 1;
+    sync_before_mma();
+    if (!__syncthreads_and(ok)) break;
+    if (t == 0) {
+      const Operand kq{smem_u32(sm + S_OFF_KQ), 0, false, 0, 0, 16384};
+      const Operand hB{smem_u32(sm + S_OFF_H_HI), smem_u32(sm + S_OFF_H_LO), true, 8192, 2048, 0};
+      issue_gemm(tmem + ST_1, kq, hB, ID_KM, 8);
+      mma_commit(bar_mma);
+    }
+    uint4 vraw[8];
+    if (t < kC) {
+      if (t < L) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.v + ((cs + t) * HV + h) * kHeadDim + vt * kVT);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) vraw[q] = src[q];
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) vraw[q] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    float nra = 0.f, nrb = 0.f;
+    if (next < end) load_gates(next, nra, nrb);
+    ok = mbar_wait(bar_mma, mma_phase);
+    mma_phase ^= 1;
+    tc_fence_after();
+    if (!__syncthreads_and(ok)) break;
+
+    const float g_last = sG[kC - 1];
+    if (t < kC) {
+      // X row j = t: V_j - gamma_j (K H)_j, into the dead Q half of the tile
+      float xr[64];
+      tmem_ld64(trow + ST_1, xr);
+      const float gam = ex2(sG[t]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t w[4] = {vraw[q].x, vraw[q].y, vraw[q].z, vraw[q].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          xr[q * 8 + 2 * e] = __uint_as_float(w[e] << 16) - gam * xr[q * 8 + 2 * e];
+          xr[q * 8 + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u) - gam * xr[q * 8 + 2 * e + 1];
+        }
+      }
+      store_row_split(sm + S_OFF_X_HI, sm + S_OFF_X_LO, t, xr);
+    }
+
+    // ---- [U; O'] = [T_b; P] X ---------------------------------------------------------
+    ok = mbar_wait(bar_a2, a2_phase);
+    a2_phase ^= 1;
+    sync_before_mma();
+    if (!__syncthreads_and(ok)) break;
+    if (t == 0) {
+      const Operand a2{smem_u32(sm + S_OFF_A2_HI), smem_u32(sm + S_OFF_A2_LO), false, 0, 0, 0};
+      const Operand xb{smem_u32(sm + S_OFF_X_HI), smem_u32(sm + S_OFF_X_LO), true, 8192, 2048, 0};
+      issue_gemm(tmem + ST_2, a2, xb, ID_KM, 4);
+      mma_commit(bar_mma);
+    }
+    ok = mbar_wait(bar_mma, mma_phase);
+    mma_phase ^= 1;
+    tc_fence_after();
+    if (!__syncthreads_and(ok)) break;
+    if (t == 0 && next < end) issue_a2(c + 1);  // [T_b; P] of this chunk is consumed
+    if (t < kC) {
+      float u[64];
+      tmem_ld64(trow + ST_2, u);
+      const float f = (t < L) ? ex2(g_last - sG[t]) : 0.0f;
+#pragma unroll
+      for (int v = 0; v < kVT; ++v) u[v] *= f;
+      store_row_split(sm + S_OFF_X_HI, sm + S_OFF_X_LO, t, u);
+    } else {
+      const int i = t - kC;
+      float o[64], qhv[64];
+      tmem_ld64(trow + ST_2, o);
+      tmem_ld64(trow + ST_1, qhv);
+      if (i < L) {
+        const float gam = ex2(sG[i]);
+        __nv_bfloat16* dst = p.out + ((cs + i) * HV + h) * kHeadDim + vt * kVT;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int v0 = q * 8 + 2 * e;
+            const float o0 = p.scale * fmaf(gam, qhv[v0], o[v0]);
+            const float o1 = p.scale * fmaf(gam, qhv[v0 + 1], o[v0 + 1]);
+            w[e] = pack_bf16(__float2bfloat16_rn(o0), __float2bfloat16_rn(o1));
+          }
+          *reinterpret_cast<uint4*>(dst + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+
+    // ---- dH = K^T diag(f) U;  H <- gamma_last H + dH -----------------------------------------
+    sync_before_mma();
+    if (t == 0) {
+      const Operand kt{smem_u32(sm + S_OFF_KQ), 0, true, 16384, 2048, 0};
+      const Operand ub{smem_u32(sm + S_OFF_X_HI), smem_u32(sm + S_OFF_X_LO), true, 8192, 2048, 0};
+      issue_gemm(tmem + ST_2, kt, ub, ID_MM, 4);
+      mma_commit(bar_mma);
+    }
+    ok = mbar_wait(bar_mma, mma_phase);
+    mma_phase ^= 1;
+    tc_fence_after();
+    if (!__syncthreads_and(ok)) break;
+    if (t == 0 && next < end) issue_tma(next);
+    {
+      float dh[64];
+      tmem_ld64(trow + ST_2, dh);
+      tmem_ld64(trow + ST_H, hrow);
+      const float gl = ex2(g_last);
+#pragma unroll
+      for (int v = 0; v < kVT; ++v) hrow[v] = fmaf(gl, hrow[v], dh[v]);
+      tmem_st64(trow + ST_H, hrow);
+      store_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, t, hrow);
+    }
+    ra = nra;
+    rb = nrb;
+  }
+
+  if (ok) {
+    tmem_ld64(trow + ST_H, hrow);
+#pragma unroll
+    for (int v = 0; v < kVT; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
+  } else if (t == 0 && p.status) {
+    atomicExch(p.status, 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kScanTmemCols);
+}
+
+}  // namespace
+
+size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV) {
+  const size_t head = (256 + 8 * static_cast<size_t>(N + 1) + 1023) & ~size_t(1023);
+  const size_t chunks = static_cast<size_t>((T + kC - 1) / kC + N);
+  return head + chunks * static_cast<size_t>(HV) * kA2Bytes;
+}
+
+int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_t stream) {
+  if (p.N == 0) return 0;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int64_t* offs = reinterpret_cast<int64_t*>(ws + 256);
+  const size_t head = (256 + 8 * static_cast<size_t>(p.N + 1) + 1023) & ~size_t(1023);
+  uint8_t* a2 = ws + head;
+  ChunkTmaps maps;
+  const int64_t Tm = p.T > 0 ? p.T : 1;
+  const void* kb = p.T > 0 ? static_cast<const void*>(p.k) : static_cast<const void*>(p.new_state);
+  const void* qb = p.T > 0 ? static_cast<const void*>(p.q) : static_cast<const void*>(p.new_state);
+  if (!encode_qk_map(&maps.k, kb, Tm, p.HQ) || !encode_qk_map(&maps.q, qb, Tm, p.HQ)) return -2;
+  if (cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem) !=
+          cudaSuccess)
+    return -1;
+  chunk_offsets_kernel<<<1, 1024, 0, stream>>>(p, offs);
+  const int64_t cap = (p.T + kC - 1) / kC + p.N;
+  if (p.T > 0) {
+    prep_kernel<<<static_cast<unsigned>(cap * p.HV), 128, kPrepSmem, stream>>>(p, maps, offs, a2);
+  }
+  scan_kernel<<<static_cast<unsigned>(p.N * p.HV * kTiles), 128, kScanSmem, stream>>>(p, maps,
+                                                                                     offs, a2);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace gdn

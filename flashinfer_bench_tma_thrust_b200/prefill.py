@@ -104,8 +104,10 @@ _workspaces: dict = {}
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-device workspace of the chunked kernel (zeroed once; holds the sticky
-    status word). Grown on demand, never shrunk."""
+    """Per-device workspace of the chunked prefill (zeroed once; its first bytes hold
+    the sticky status word, the rest the per-chunk [T_b; P] operands of the two-phase
+    path, 24 KB per (chunk, v-head)). Grown on demand, never shrunk; calls on one
+    device share it, so they must be ordered on one stream."""
     key = (device.type, device.index)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
@@ -130,17 +132,27 @@ def _aligned(t):
     return t if t.numel() == 0 or t.data_ptr() % 16 == 0 else t.clone()
 
 
-def run_chunked(P: _Prepared, out, new_state):
+_FUSED_WORKSPACE_BYTES = 256
+
+
+def run_chunked(P: _Prepared, out, new_state, fused: bool = False):
+    """Chunked tensor-core prefill. With the full workspace the C library runs the
+    two-phase path (parallel prep of the per-chunk [T_b; P] operands, then the state
+    scan); ``fused=True`` hands it only 256 bytes, which selects the single-kernel path."""
     lib = _lib.load()
     q, k, v = _aligned(P.q), _aligned(P.k), _aligned(P.v)
-    nbytes = lib.gdn_prefill_chunked_workspace_size(P.T, P.N, P.HV)
-    ws = workspace(P.dev, nbytes)
+    if fused:
+        ws = workspace(P.dev, _FUSED_WORKSPACE_BYTES)
+        nbytes = _FUSED_WORKSPACE_BYTES
+    else:
+        nbytes = lib.gdn_prefill_chunked_workspace_size(P.T, P.N, P.HV)
+        ws = workspace(P.dev, nbytes)
     with torch.cuda.device(P.dev):
         rc = lib.gdn_prefill_chunked_fwd(
             _ptr0(q), _ptr0(k), _ptr0(v), C.ptr(P.state),
             P.A.data_ptr(), P.A_t, _ptr0(P.a), P.a_t, P.d.data_ptr(), P.d_t, _ptr0(P.b), P.b_t,
             P.cu.data_ptr(), P.cu_t, P.scale, _ptr0(out), _ptr0(new_state),
-            P.T, P.N, P.HQ, P.HV, P.D, ws.data_ptr(), ws.numel(), C.stream_handle(P.dev))
+            P.T, P.N, P.HQ, P.HV, P.D, ws.data_ptr(), nbytes, C.stream_handle(P.dev))
     _lib.check(rc, "gdn_prefill_chunked_fwd")
     return out, new_state
 
@@ -153,6 +165,13 @@ def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
     return run_chunked(P, out, new_state)
 
 
+def kernel_fused(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
+    """Chunked prefill on the single-kernel path (needs only a 256-byte workspace)."""
+    P = prepare(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+    out, new_state = _alloc_outputs(P)
+    return run_chunked(P, out, new_state, fused=True)
+
+
 def launches_per_call() -> int:
-    """Kernel launches one ``kernel()`` call makes (reported by the benchmark)."""
-    return 1
+    """Kernel launches one ``kernel()`` call makes (chunk offsets, prep, scan)."""
+    return 3

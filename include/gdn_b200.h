@@ -119,13 +119,16 @@ GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* 
  * over chunks); semantics of gdn/prefill/baseline/triton/kernel.py:18-100.
  * Arguments as gdn_prefill_recurrent_fwd, plus:
  *
- *   workspace        device memory of at least
- *                    gdn_prefill_chunked_workspace_size(T, N, HV) bytes, 16-byte
- *                    aligned, zeroed once by the caller before its first use. It
- *                    holds a sticky status word that the kernel sets to 1 if one of
- *                    its bounded waits gave up (read it with
- *                    gdn_prefill_chunked_status). Calls that share a workspace
- *                    must be stream-ordered.
+ *   workspace        device memory, 16-byte aligned, zeroed once by the caller
+ *                    before its first use. With at least
+ *                    gdn_prefill_chunked_workspace_size(T, N, HV) bytes the call
+ *                    runs the two-phase path (a parallel prep kernel over all
+ *                    (chunk, v-head) pairs writes 24 KB per pair, then the state
+ *                    scan); with less, but at least 256 bytes, it runs the fused
+ *                    single-kernel path. The first 4 bytes are a sticky status
+ *                    word that a kernel sets to 1 if one of its bounded waits gave
+ *                    up (read it with gdn_prefill_chunked_status). Calls that
+ *                    share a workspace must be stream-ordered.
  *
  * q, k, v and out must be 16-byte aligned (q/k are read by TMA); T < 2^31.
  * One launch per call; the work runs in fp32 on the state with tensor-core
@@ -158,8 +161,8 @@ GDN_API int gdn_prefill_chunked_status(const void* workspace, int* host_status, 
  * - The first call on a device (with that device current) looks up the
  *   array's device address once; make that first call before any stream
  *   capture on that device.
- * - Returns GDN_ERR_WORKSPACE if a call would need more than 4096 bytes of
- *   scratch (the current kernel needs 256, independent of T, N and HV).
+ * - Runs the fused single-kernel path, whose scratch is 256 bytes for any T,
+ *   N and HV; returns GDN_ERR_WORKSPACE if a call would need more than 4096.
  * - All calls share the one array, which keeps the previous call's contents;
  *   each call zeroes the part it uses with a memset on `stream`. Calls whose
  *   work overlaps on the GPU (different streams without ordering) race on it.

@@ -12,7 +12,8 @@ from parity import (PREFILL_STATE_ATOL, STATE_REL_FROB, assert_out_close, assert
 pytestmark = pytest.mark.gpu
 
 PRE_CASES = [c for c in golden.case_names() if c.startswith("pre_")]
-IMPLS = {"chunked": prefill.kernel, "recurrent": prefill.kernel_recurrent}
+IMPLS = {"chunked": prefill.kernel, "fused": prefill.kernel_fused,
+         "recurrent": prefill.kernel_recurrent}
 
 
 @pytest.mark.parametrize("impl", sorted(IMPLS))
@@ -80,8 +81,11 @@ def test_chunked_vs_recurrent_varlen_config():
     x = W.prefill_inputs(lengths, seed=21, gen_device="cuda", device="cuda")
     o1, s1 = prefill.kernel(*x.args())
     o2, s2 = prefill.kernel_recurrent(*x.args())
+    o3, s3 = prefill.kernel_fused(*x.args())
     assert_out_close(o1, o2, "chunked vs recurrent")
     assert_state_close(s1, s2, PREFILL_STATE_ATOL, "chunked vs recurrent")
+    assert_out_close(o3, o2, "fused vs recurrent")
+    assert_state_close(s3, s2, PREFILL_STATE_ATOL, "fused vs recurrent")
 
 
 def test_chunked_status_word_clean():
