@@ -26,6 +26,18 @@ __device__ __forceinline__ int fidx(int r, int c) {
   return r * 64 + ((((c >> 2) ^ r) & 15) << 2) + (c & 3);
 }
 
+// Layouts of the fp32 64 x 64 solve matrices. SwzLayout: stride 64 with the 16-byte
+// column groups XOR-swizzled by row (16 KB, for kernels short of shared memory).
+// PadLayout: stride 68 (17 KB): addresses are affine in the column, so unrolled loops
+// fold them into immediates, and row-per-thread float4 writes stay conflict-free.
+struct SwzLayout {
+  static __device__ __forceinline__ int idx(int r, int c) { return fidx(r, c); }
+};
+struct PadLayout {
+  static __device__ __forceinline__ int idx(int r, int c) { return r * 68 + c; }
+};
+
+
 constexpr uint32_t ID_KK = idesc_bf16(128, 64, false, false);  // A K-major, B K-major
 constexpr uint32_t ID_KM = idesc_bf16(128, 64, false, true);   // A K-major, B MN-major
 constexpr uint32_t ID_MM = idesc_bf16(128, 64, true, true);    // A MN-major, B MN-major
@@ -135,10 +147,36 @@ __device__ __forceinline__ void chunk_gates(float ra, float rb, int L, float A_l
 
 }
 
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// chunk_gates for warps 0 and 1 only (threads 0..63), synchronised with a named
+// barrier so that the other warps can work meanwhile. Readers of sG / sBeta in
+// other warps must pass a block-wide barrier afterwards.
+__device__ __forceinline__ void chunk_gates_w01(float ra, float rb, int L, float A_log,
+                                                float dtb, float* sG, float* sBeta) {
+  const int t = threadIdx.x, lane = t & 31;
+  const bool valid = t < L;
+  const float lg = valid ? gate_log_decay(A_log, ra, dtb) * kLog2e : 0.0f;
+  const float beta = valid ? gate_beta(rb) : 0.0f;
+  float x = lg;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (t < 32) sG[t] = x;
+  sBeta[t] = beta;
+  named_bar_sync(1, 64);
+  if (t >= 32) sG[t] = x + sG[31];
+}
+
 // From S = [K;Q] K^T in TMEM (this thread's lane): thread t < 64 writes row t of
 // A = strict_lower(beta_i e^{Gamma_i-Gamma_j} S_kk) (fp32, for the solve) and the
 // identity row t of [I; M]; thread t >= 64 writes row t of [I; M] with
 // M = lower(e^{Gamma_i-Gamma_j} S_qk), as bf16 hi/lo K-major rows.
+template <class Lay>
 __device__ __forceinline__ void build_a_m(uint32_t ts_row, float* sAf, const float* sG,
                                           const float* sBeta, uint8_t* a2_hi, uint8_t* a2_lo) {
   const int t = threadIdx.x;
@@ -155,11 +193,17 @@ __device__ __forceinline__ void build_a_m(uint32_t ts_row, float* sAf, const flo
         w.y = (j + 1 < t) ? bi * ex2(gi - sG[j + 1]) * srow[j + 1] : 0.f;
         w.z = (j + 2 < t) ? bi * ex2(gi - sG[j + 2]) * srow[j + 2] : 0.f;
         w.w = (j + 3 < t) ? bi * ex2(gi - sG[j + 3]) * srow[j + 3] : 0.f;
-        *reinterpret_cast<float4*>(sAf + fidx(t, j)) = w;
+        *reinterpret_cast<float4*>(sAf + Lay::idx(t, j)) = w;
       }
+      // identity row: one nonzero bf16 (1.0 = 0x3f80) in chunk t/8; lo half is zero
 #pragma unroll
-      for (int j = 0; j < kC; ++j) srow[j] = (j == t) ? 1.0f : 0.0f;
-      store_row_split(a2_hi, a2_lo, t, srow);
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if (c == (t >> 3)) w[(t & 7) >> 1] = (t & 1) ? 0x3f800000u : 0x00003f80u;
+        const uint32_t off = sw128_chunk(t, c);
+        *reinterpret_cast<uint4*>(a2_hi + off) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(a2_lo + off) = make_uint4(0u, 0u, 0u, 0u);
+      }
     } else {
       // M row i = t - 64
       const int i = t - kC;
@@ -171,13 +215,67 @@ __device__ __forceinline__ void build_a_m(uint32_t ts_row, float* sAf, const flo
   }
 }
 
+// One warp: W = A_{I,K} T_{K,J} (16 x 16 x 16) stored into the scratch block at
+// block coordinates (sr, sc). Lane owns row lane/2 and 8 columns.
+template <class Lay>
+__device__ __forceinline__ void solve_partial(const float* sAf, float* sTf, int I, int K, int J,
+                                              int sr, int sc, int lane) {
+  const int r = lane >> 1, c0 = (lane & 1) * 8;
+  float w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) w[e] = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float a = sAf[Lay::idx(16 * I + r, 16 * K + k)];
+    const float4 t0 = *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * K + k, 16 * J + c0));
+    const float4 t1 =
+        *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * K + k, 16 * J + c0 + 4));
+    w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
+    w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
+    w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
+    w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
+  }
+  *reinterpret_cast<float4*>(sTf + Lay::idx(16 * sr + r, 16 * sc + c0)) =
+      make_float4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<float4*>(sTf + Lay::idx(16 * sr + r, 16 * sc + c0 + 4)) =
+      make_float4(w[4], w[5], w[6], w[7]);
+}
+
+// T_IJ = -T_II (sum of NP scratch blocks), computed by a group of G threads (g = rank
+// in the group): each owns 256/G outputs of one row.
+template <class Lay, int NP, int G>
+__device__ __forceinline__ void solve_finish(float* sTf, int I, int J, int sr0, int sc0, int sr1,
+                                             int sc1, int sr2, int sc2, int g) {
+  constexpr int kCols = 256 / G;  // 8, 4 or 2 columns per thread
+  constexpr int kPerRow = 16 / kCols;
+  const int r = g / kPerRow, c0 = (g % kPerRow) * kCols;
+  float w[kCols];
+#pragma unroll
+  for (int e = 0; e < kCols; ++e) w[e] = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float a = sTf[Lay::idx(16 * I + r, 16 * I + k)];
+#pragma unroll
+    for (int e = 0; e < kCols; ++e) {
+      w[e] = fmaf(a, sTf[Lay::idx(16 * sr0 + k, 16 * sc0 + c0 + e)], w[e]);
+      if (NP > 1) w[e] = fmaf(a, sTf[Lay::idx(16 * sr1 + k, 16 * sc1 + c0 + e)], w[e]);
+      if (NP > 2) w[e] = fmaf(a, sTf[Lay::idx(16 * sr2 + k, 16 * sc2 + c0 + e)], w[e]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < kCols; ++e) sTf[Lay::idx(16 * I + r, 16 * J + c0 + e)] = -w[e];
+}
+
 // T_b = (I + A)^-1 diag(beta), written as the MN-major bf16 hi/lo B operand (rows j,
-// cols n). A: strictly lower 64 x 64 fp32 in sAf (fidx layout); sTf receives T, its
-// upper blocks serve as scratch. Block-wide: every thread of the 128 calls it.
+// cols n). A: strictly lower 64 x 64 fp32 in sAf; sTf receives T, its upper blocks
+// serve as scratch for the partial products. Blocked by 16: the four diagonal blocks
+// by forward substitution (one warp each), then the off-diagonal blocks by distance,
+// T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ, with the partial products of one block
+// spread over warps. Block-wide: all 128 threads call it.
+template <class Lay>
 __device__ __forceinline__ void solve_tb(float* sAf, float* sTf, const float* sBeta,
                                          uint8_t* tb_hi, uint8_t* tb_lo) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  // ---- T = (I + A)^-1, blocked 16 x 16 ---------------------------------------------
   if (lane < 16) {
     const int b0 = warp * 16;
     float tc[16];
@@ -185,72 +283,50 @@ __device__ __forceinline__ void solve_tb(float* sAf, float* sTf, const float* sB
     for (int i = 0; i < 16; ++i) {
       float s = 0.f;
 #pragma unroll
-      for (int j = 0; j < i; ++j) s = fmaf(sAf[fidx(b0 + i, b0 + j)], tc[j], s);
+      for (int j = 0; j < i; ++j) s = fmaf(sAf[Lay::idx(b0 + i, b0 + j)], tc[j], s);
       tc[i] = (i < lane) ? 0.f : ((i == lane) ? 1.f : -s);
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) sTf[fidx(b0 + i, b0 + lane)] = tc[i];
+    for (int i = 0; i < 16; ++i) sTf[Lay::idx(b0 + i, b0 + lane)] = tc[i];
   }
   __syncthreads();
-  // Off-diagonal blocks by distance d = I - J: one warp per block, each lane
-  // owns row r = lane/2 and 8 columns c0 = 8*(lane&1) of the 16 x 16 block.
-  {
-    const int r = lane >> 1, c0 = (lane & 1) * 8;
-    for (int d = 1; d < 4; ++d) {
-      const int I = d + warp, J = warp;
-      float w[8];
-      if (warp < 4 - d) {  // W_IJ = sum_{K=J}^{I-1} A_IK T_KJ  -> scratch block (J, I)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) w[e] = 0.f;
-        for (int K = J; K < I; ++K) {
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float a = sAf[fidx(16 * I + r, 16 * K + k)];
-            const float4 t0 = *reinterpret_cast<const float4*>(sTf + fidx(16 * K + k, 16 * J + c0));
-            const float4 t1 = *reinterpret_cast<const float4*>(sTf + fidx(16 * K + k, 16 * J + c0 + 4));
-            w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
-            w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
-            w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
-            w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
-          }
-        }
-        *reinterpret_cast<float4*>(sTf + fidx(16 * J + r, 16 * I + c0)) =
-            make_float4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<float4*>(sTf + fidx(16 * J + r, 16 * I + c0 + 4)) =
-            make_float4(w[4], w[5], w[6], w[7]);
-      }
-      __syncwarp();
-      if (warp < 4 - d) {  // T_IJ = -T_II W_IJ (W read back from the scratch block)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) w[e] = 0.f;
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float a = sTf[fidx(16 * I + r, 16 * I + k)];
-          const float4 t0 = *reinterpret_cast<const float4*>(sTf + fidx(16 * J + k, 16 * I + c0));
-          const float4 t1 = *reinterpret_cast<const float4*>(sTf + fidx(16 * J + k, 16 * I + c0 + 4));
-          w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
-          w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
-          w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
-          w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
-        }
-        *reinterpret_cast<float4*>(sTf + fidx(16 * I + r, 16 * J + c0)) =
-            make_float4(-w[0], -w[1], -w[2], -w[3]);
-        *reinterpret_cast<float4*>(sTf + fidx(16 * I + r, 16 * J + c0 + 4)) =
-            make_float4(-w[4], -w[5], -w[6], -w[7]);
-      }
-      __syncthreads();
-    }
+  // distance 1: blocks (1,0), (2,1), (3,2), one warp each; scratch (J, I)
+  if (warp < 3) {
+    const int I = warp + 1, J = warp;
+    solve_partial<Lay>(sAf, sTf, I, J, J, J, I, lane);
+    __syncwarp();
+    solve_finish<Lay, 1, 32>(sTf, I, J, J, I, 0, 0, 0, 0, lane);
   }
+  __syncthreads();
+  // distance 2: blocks (2,0) [warps 0,1] and (3,1) [warps 2,3]; one partial per warp
+  {
+    const int b = warp >> 1, I = 2 + b, J = b, K = J + (warp & 1);
+    // scratch: (J, I) for K = J, (J, J+1) for K = J+1 (free since distance 1 finished)
+    solve_partial<Lay>(sAf, sTf, I, K, J, J, (warp & 1) ? J + 1 : I, lane);
+  }
+  __syncthreads();
+  {
+    const int b = warp >> 1, I = 2 + b, J = b;
+    solve_finish<Lay, 2, 64>(sTf, I, J, J, I, J, J + 1, 0, 0, t & 63);
+  }
+  __syncthreads();
+  // distance 3: block (3,0); partials K = 0, 1, 2 on warps 0..2 into (0,3), (0,1), (0,2)
+  if (warp < 3) solve_partial<Lay>(sAf, sTf, 3, warp, 0, 0, warp == 0 ? 3 : warp, lane);
+  __syncthreads();
+  {
+    solve_finish<Lay, 3, 128>(sTf, 3, 0, 0, 3, 0, 1, 0, 2, t);
+  }
+  __syncthreads();
   {
     // T_b = T diag(beta) as the MN-major B operand: row j, cols n (half of the row per
-    // thread); written over A, which the solve no longer needs
+    // thread)
     const int j = t & (kC - 1), half = t >> 6;
     float vals[32];
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
       const int nn = half * 32 + c;
       const bool lower = (nn >> 4) < (j >> 4) || ((nn >> 4) == (j >> 4) && nn <= j);
-      vals[c] = lower ? sTf[fidx(j, nn)] * sBeta[nn] : 0.f;
+      vals[c] = lower ? sTf[Lay::idx(j, nn)] * sBeta[nn] : 0.f;
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -268,7 +344,6 @@ __device__ __forceinline__ void solve_tb(float* sAf, float* sTf, const float* sB
       *reinterpret_cast<uint4*>(tb_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
   }
-
 }
 
 struct ChunkTmaps {

@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(128, 2)
 
     PHASE(2);  // S, G1 MMA
     const float g_last = sG[kC - 1];
-    build_a_m(trow + TM_S, sAf, sG, sBeta, sm + OFF_A2_HI, sm + OFF_A2_LO);
+    build_a_m<SwzLayout>(trow + TM_S, sAf, sG, sBeta, sm + OFF_A2_HI, sm + OFF_A2_LO);
     if (t < kC) {
       // X row j = t:  V_j - gamma_j (K H)_j, into the dead Q half of the tile
       float xr[64];
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(128, 2)
     float nra = 0.f, nrb = 0.f;
     if (next < end) load_gates(next, end, nra, nrb);
 
-    solve_tb(sAf, sTf, sBeta, sm + OFF_TB_HI, sm + OFF_TB_LO);
+    solve_tb<SwzLayout>(sAf, sTf, sBeta, sm + OFF_TB_HI, sm + OFF_TB_LO);
     PHASE(6);  // T_b write
     // ---- [T_b; P] = [I; M] T_b -----------------------------------------------------
     sync_before_mma();

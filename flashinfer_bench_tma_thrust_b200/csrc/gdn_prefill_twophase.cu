@@ -30,7 +30,24 @@ namespace {
 using namespace sm100;
 using namespace chunk;
 
-constexpr uint32_t kA2Bytes = 24576;  // per (chunk, v-head): hi 16 KB + lo rows 0..63 8 KB
+constexpr uint32_t kA2Bytes = 24576;
+
+#ifdef GDN_PHASE_PROFILE
+// Debug-only phase timer of the scan (block 0, thread 0): clock64 deltas per phase.
+__device__ long long g_scan_cycles[16];
+#define SPHASE(i)                                     \
+  do {                                                \
+    if (blockIdx.x == 0 && threadIdx.x == 0) {        \
+      const long long now_ = clock64();               \
+      g_scan_cycles[i] += now_ - sphase_last_;        \
+      sphase_last_ = now_;                            \
+    }                                                 \
+  } while (0)
+#else
+#define SPHASE(i) \
+  do {            \
+  } while (0)
+#endif  // per (chunk, v-head): hi 16 KB + lo rows 0..63 8 KB
 
 __device__ __forceinline__ void seq_bounds(const PrefillParams& p, int64_t n, int64_t& start,
                                            int64_t& end) {
@@ -87,19 +104,20 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
 }
 
 // ------------------------------------------------------------------ prep
-// Shared memory: KQ tile (32 KB, TMA) — dead after S, then the fp32 A (0..16 KB)
-// and T (16..32 KB) of the solve, then T_b hi/lo over A; [I; M] hi/lo (32 KB).
+// Shared memory: KQ tile (32 KB, TMA) — dead after S, then the fp32 A and T of the
+// solve (padded rows, 17 KB each; T spills 2 KB past the tile), then T_b hi/lo over
+// A; [I; M] hi/lo (32 KB).
 constexpr uint32_t P_OFF_KQ = 0;
 constexpr uint32_t P_OFF_AF = 0;
-constexpr uint32_t P_OFF_TF = 16384;
+constexpr uint32_t P_OFF_TF = 17408;
 constexpr uint32_t P_OFF_TB_HI = 0;
 constexpr uint32_t P_OFF_TB_LO = 8192;
-constexpr uint32_t P_OFF_A2_HI = 32768;
-constexpr uint32_t P_OFF_A2_LO = 49152;
-constexpr uint32_t P_OFF_G = 65536;
-constexpr uint32_t P_OFF_BETA = 65792;
-constexpr uint32_t P_OFF_BAR = 66048;
-constexpr uint32_t kPrepSmem = 66112 + 1024;
+constexpr uint32_t P_OFF_A2_HI = 35840;   // 1024-aligned, after T
+constexpr uint32_t P_OFF_A2_LO = 52224;
+constexpr uint32_t P_OFF_G = 68608;
+constexpr uint32_t P_OFF_BETA = 68864;
+constexpr uint32_t P_OFF_BAR = 69120;
+constexpr uint32_t kPrepSmem = 69184 + 1024;
 constexpr uint32_t kPrepTmemCols = 128;
 constexpr uint32_t PT_S = 0, PT_P = 64;
 
@@ -174,9 +192,9 @@ __global__ void __launch_bounds__(128, 3)
     tc_fence_after();
     if (__syncthreads_and(ok)) {
       // the K/Q tile is dead: A, T and T_b reuse its space
-      build_a_m(trow + PT_S, sAf, sG, sBeta, sm + P_OFF_A2_HI, sm + P_OFF_A2_LO);
+      build_a_m<PadLayout>(trow + PT_S, sAf, sG, sBeta, sm + P_OFF_A2_HI, sm + P_OFF_A2_LO);
       __syncthreads();
-      solve_tb(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
+      solve_tb<PadLayout>(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
       sync_before_mma();
       if (t == 0) {
         const Operand a2{smem_u32(sm + P_OFF_A2_HI), smem_u32(sm + P_OFF_A2_LO), false, 0, 0, 0};
@@ -220,6 +238,8 @@ __global__ void __launch_bounds__(128, 3)
 // ------------------------------------------------------------------ scan
 // Shared memory: KQ tile (32 KB; its Q halves hold X and then diag(f) U),
 // H hi/lo (32 KB), [T_b; P] hi/lo (32 KB; lo rows 64..127 stay zero).
+// 256 threads: thread t owns TMEM lane / operand row r = t % 128 and the 32
+// columns [32 c, 32 c + 32) of it, c = t / 128 (warps w and w + 4 share lanes).
 constexpr uint32_t S_OFF_KQ = 0;
 constexpr uint32_t S_OFF_X_HI = 8192;
 constexpr uint32_t S_OFF_X_LO = 24576;
@@ -227,27 +247,58 @@ constexpr uint32_t S_OFF_H_HI = 32768;
 constexpr uint32_t S_OFF_H_LO = 49152;
 constexpr uint32_t S_OFF_A2_HI = 65536;
 constexpr uint32_t S_OFF_A2_LO = 81920;
-constexpr uint32_t S_OFF_G = 98304;
-constexpr uint32_t S_OFF_BETA = 98560;
-constexpr uint32_t S_OFF_BAR = 98816;
-constexpr uint32_t kScanSmem = 98880 + 1024;
+constexpr uint32_t S_OFF_G = 98304;  // 2 x 64 fp32 (double-buffered by chunk parity)
+constexpr uint32_t S_OFF_BETA = 98816;  // 2 x 64 fp32 (written by the gate scan, unused here)
+constexpr uint32_t S_OFF_BAR = 99328;
+constexpr uint32_t kScanSmem = 99392 + 1024;
 constexpr uint32_t kScanTmemCols = 256;
-constexpr uint32_t ST_H = 0, ST_1 = 64, ST_2 = 128;
+constexpr uint32_t ST_H = 0, ST_1 = 64, ST_2 = 128, ST_3 = 192;
+constexpr int kScanThreads = 256;
+constexpr int kHalf = kVT / 2;  // columns per thread
 
-__global__ void __launch_bounds__(128, 2)
+// Split 32 fp32 values into bf16 hi/lo and write them as chunks [c0, c0+4) of
+// row `row` of two 128B-swizzled tiles.
+__device__ __forceinline__ void store_half_row_split(uint8_t* hi, uint8_t* lo, uint32_t row,
+                                                     uint32_t c0, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat16 h0, l0, h1, l1;
+      split_bf16(v[c * 8 + 2 * e], h0, l0);
+      split_bf16(v[c * 8 + 2 * e + 1], h1, l1);
+      hw[e] = pack_bf16(h0, h1);
+      lw[e] = pack_bf16(l0, l1);
+    }
+    const uint32_t off = sw128_chunk(row, c0 + c);
+    *reinterpret_cast<uint4*>(hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+}
+
+__device__ __forceinline__ void tmem_ld32w(uint32_t taddr, float (&r)[32]) {
+  tmem_ld32(taddr, r);
+  tmem_ld_wait();
+}
+
+__global__ void __launch_bounds__(kScanThreads, 2)
     scan_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
                 const int64_t* __restrict__ offs, const uint8_t* __restrict__ a2_in) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  float* sG = reinterpret_cast<float*>(sm + S_OFF_G);
-  float* sBeta = reinterpret_cast<float*>(sm + S_OFF_BETA);
+  float* sG0 = reinterpret_cast<float*>(sm + S_OFF_G);
+  float* sBeta0 = reinterpret_cast<float*>(sm + S_OFF_BETA);
   uint64_t* bar_tma = reinterpret_cast<uint64_t*>(sm + S_OFF_BAR);
   uint64_t* bar_a2 = bar_tma + 1;
   uint64_t* bar_mma = bar_tma + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S_OFF_BAR + 32);
 
   const int t = threadIdx.x, warp = t >> 5;
+  const int r = t & 127;         // row / TMEM lane
+  const int ch = t >> 7;         // column half
+  const int col0 = ch * kHalf;   // first column owned
   const int64_t unit = blockIdx.x;
   const int vt = static_cast<int>(unit % kTiles);
   const int h = static_cast<int>((unit / kTiles) % p.HV);
@@ -257,13 +308,14 @@ __global__ void __launch_bounds__(128, 2)
   int64_t start, end;
   seq_bounds(p, n, start, end);
 
-  const int64_t sbase = ((n * p.HV + h) * kHeadDim + vt * kVT) * kHeadDim + t;
-  float hrow[kVT];
+  // state rows of this tile: S[n, h, vt*64 + v, k]; this thread owns k = r, v in its half
+  const int64_t sbase = ((n * p.HV + h) * kHeadDim + vt * kVT + col0) * kHeadDim + r;
+  float hrow[kHalf];
 #pragma unroll
-  for (int v = 0; v < kVT; ++v) hrow[v] = p.state ? p.state[sbase + v * kHeadDim] : 0.0f;
+  for (int v = 0; v < kHalf; ++v) hrow[v] = p.state ? p.state[sbase + v * kHeadDim] : 0.0f;
   if (end <= start) {  // empty sequence: pass the state through
 #pragma unroll
-    for (int v = 0; v < kVT; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
+    for (int v = 0; v < kHalf; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
     return;
   }
   const uint8_t* a2_seq = a2_in + static_cast<uint64_t>(offs[n]) * HV * kA2Bytes +
@@ -295,15 +347,16 @@ __global__ void __launch_bounds__(128, 2)
   }
   if (warp == 0) tmem_alloc(tmem_slot, kScanTmemCols);
   // the lo half of [T_b; P] has no P rows: rows 64..127 stay zero
-  for (int i = t; i < 8192 / 16; i += 128)
+  for (int i = t; i < 8192 / 16; i += kScanThreads)
     reinterpret_cast<uint4*>(sm + S_OFF_A2_LO + 8192)[i] = make_uint4(0u, 0u, 0u, 0u);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  tmem_st64(trow + ST_H, hrow);
-  store_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, t, hrow);
+  const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + col0;
+  tmem_st32(trow + ST_H, hrow);
+  tmem_st_wait();
+  store_half_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, r, ch * 4, hrow);
 
   const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
   const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
@@ -324,16 +377,24 @@ __global__ void __launch_bounds__(128, 2)
     issue_a2(0);
   }
   load_gates(start, ra, rb);
+  chunk_gates(ra, rb, static_cast<int>((end - start) < kC ? (end - start) : kC), A_log, dtb,
+              sG0, sBeta0);
 
   int64_t c = 0;
+#ifdef GDN_PHASE_PROFILE
+  long long sphase_last_ = clock64();
+#endif
   for (int64_t cs = start; cs < end; cs += kC, ++c) {
     const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
     const int64_t next = cs + kC;
-    chunk_gates(ra, rb, L, A_log, dtb, sG, sBeta);
+    const int buf = static_cast<int>(c & 1);
+    const float* sG = sG0 + buf * kC;  // gates of this chunk (computed during the previous one)
 
     // ---- [KH; QH] = [K;Q] H --------------------------------------------------------
+    SPHASE(0);  // loop top -> before TMA wait
     ok = mbar_wait(bar_tma, tma_phase);
     tma_phase ^= 1;
+    SPHASE(1);  // TMA wait
     sync_before_mma();
     if (!__syncthreads_and(ok)) break;
     if (t == 0) {
@@ -342,33 +403,34 @@ __global__ void __launch_bounds__(128, 2)
       issue_gemm(tmem + ST_1, kq, hB, ID_KM, 8);
       mma_commit(bar_mma);
     }
-    uint4 vraw[8];
-    if (t < kC) {
-      if (t < L) {
+    uint4 vraw[4];
+    if (r < kC) {
+      if (r < L) {
         const uint4* src = reinterpret_cast<const uint4*>(
-            p.v + ((cs + t) * HV + h) * kHeadDim + vt * kVT);
+            p.v + ((cs + r) * HV + h) * kHeadDim + vt * kVT + col0);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) vraw[q] = src[q];
+        for (int q = 0; q < 4; ++q) vraw[q] = src[q];
       } else {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) vraw[q] = make_uint4(0u, 0u, 0u, 0u);
+        for (int q = 0; q < 4; ++q) vraw[q] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
     float nra = 0.f, nrb = 0.f;
     if (next < end) load_gates(next, nra, nrb);
+    SPHASE(2);  // G1 issue + V/gate loads
     ok = mbar_wait(bar_mma, mma_phase);
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
 
     const float g_last = sG[kC - 1];
-    if (t < kC) {
-      // X row j = t: V_j - gamma_j (K H)_j, into the dead Q half of the tile
-      float xr[64];
-      tmem_ld64(trow + ST_1, xr);
-      const float gam = ex2(sG[t]);
+    if (r < kC) {
+      // X row j = r: V_j - gamma_j (K H)_j, into the dead Q half of the tile
+      float xr[32];
+      tmem_ld32w(trow + ST_1, xr);
+      const float gam = ex2(sG[r]);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 4; ++q) {
         const uint32_t w[4] = {vraw[q].x, vraw[q].y, vraw[q].z, vraw[q].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -376,12 +438,14 @@ __global__ void __launch_bounds__(128, 2)
           xr[q * 8 + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u) - gam * xr[q * 8 + 2 * e + 1];
         }
       }
-      store_row_split(sm + S_OFF_X_HI, sm + S_OFF_X_LO, t, xr);
+      store_half_row_split(sm + S_OFF_X_HI, sm + S_OFF_X_LO, r, ch * 4, xr);
     }
+    SPHASE(3);  // G1 wait + X build
 
     // ---- [U; O'] = [T_b; P] X ---------------------------------------------------------
     ok = mbar_wait(bar_a2, a2_phase);
     a2_phase ^= 1;
+    SPHASE(4);  // A2 wait
     sync_before_mma();
     if (!__syncthreads_and(ok)) break;
     if (t == 0) {
@@ -390,28 +454,45 @@ __global__ void __launch_bounds__(128, 2)
       issue_gemm(tmem + ST_2, a2, xb, ID_KM, 4);
       mma_commit(bar_mma);
     }
+    SPHASE(5);  // G2 issue
     ok = mbar_wait(bar_mma, mma_phase);
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
     if (t == 0 && next < end) issue_a2(c + 1);  // [T_b; P] of this chunk is consumed
-    if (t < kC) {
-      float u[64];
-      tmem_ld64(trow + ST_2, u);
-      const float f = (t < L) ? ex2(g_last - sG[t]) : 0.0f;
+    if (r < kC) {
+      // f_j U_j with f_j = e^{Gamma_last - Gamma_j} (0 for padded rows): the state
+      // update then reads the raw K tile, dH = K^T diag(f) U
+      float u[32];
+      tmem_ld32w(trow + ST_2, u);
+      const float f = (r < L) ? ex2(g_last - sG[r]) : 0.0f;
 #pragma unroll
-      for (int v = 0; v < kVT; ++v) u[v] *= f;
-      store_row_split(sm + S_OFF_X_HI, sm + S_OFF_X_LO, t, u);
-    } else {
-      const int i = t - kC;
-      float o[64], qhv[64];
-      tmem_ld64(trow + ST_2, o);
-      tmem_ld64(trow + ST_1, qhv);
+      for (int v = 0; v < kHalf; ++v) u[v] *= f;
+      store_half_row_split(sm + S_OFF_X_HI, sm + S_OFF_X_LO, r, ch * 4, u);
+    }
+    SPHASE(6);  // G2 wait + U build
+
+    // ---- dH = K^T diag(f) U (into its own TMEM columns, so O' stays readable) -------------
+    sync_before_mma();
+    if (t == 0) {
+      const Operand kt{smem_u32(sm + S_OFF_KQ), 0, true, 16384, 2048, 0};
+      const Operand ub{smem_u32(sm + S_OFF_X_HI), smem_u32(sm + S_OFF_X_LO), true, 8192, 2048, 0};
+      issue_gemm(tmem + ST_3, kt, ub, ID_MM, 4);
+      mma_commit(bar_mma);
+    }
+    // while the MMA runs: rows 64..127 produce the output, warps 0-1 the gates of the
+    // next chunk (into the other gate buffer)
+    if (r >= kC) {
+      const int i = r - kC;
+      float o[32], qhv[32];
+      tmem_ld32(trow + ST_2, o);
+      tmem_ld32(trow + ST_1, qhv);
+      tmem_ld_wait();
       if (i < L) {
         const float gam = ex2(sG[i]);
-        __nv_bfloat16* dst = p.out + ((cs + i) * HV + h) * kHeadDim + vt * kVT;
+        __nv_bfloat16* dst = p.out + ((cs + i) * HV + h) * kHeadDim + vt * kVT + col0;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -423,39 +504,36 @@ __global__ void __launch_bounds__(128, 2)
           *reinterpret_cast<uint4*>(dst + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+    } else if (t < kC && next < end) {
+      const int nL = static_cast<int>((end - next) < kC ? (end - next) : kC);
+      chunk_gates_w01(nra, nrb, nL, A_log, dtb, sG0 + (buf ^ 1) * kC, sBeta0 + (buf ^ 1) * kC);
     }
-
-    // ---- dH = K^T diag(f) U;  H <- gamma_last H + dH -----------------------------------------
-    sync_before_mma();
-    if (t == 0) {
-      const Operand kt{smem_u32(sm + S_OFF_KQ), 0, true, 16384, 2048, 0};
-      const Operand ub{smem_u32(sm + S_OFF_X_HI), smem_u32(sm + S_OFF_X_LO), true, 8192, 2048, 0};
-      issue_gemm(tmem + ST_2, kt, ub, ID_MM, 4);
-      mma_commit(bar_mma);
-    }
+    SPHASE(7);  // G3 issue + O + next gates
     ok = mbar_wait(bar_mma, mma_phase);
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
+    SPHASE(8);  // G3 wait
     if (t == 0 && next < end) issue_tma(next);
     {
-      float dh[64];
-      tmem_ld64(trow + ST_2, dh);
-      tmem_ld64(trow + ST_H, hrow);
+      float dh[32];
+      tmem_ld32(trow + ST_3, dh);
+      tmem_ld32(trow + ST_H, hrow);
+      tmem_ld_wait();
       const float gl = ex2(g_last);
 #pragma unroll
-      for (int v = 0; v < kVT; ++v) hrow[v] = fmaf(gl, hrow[v], dh[v]);
-      tmem_st64(trow + ST_H, hrow);
-      store_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, t, hrow);
+      for (int v = 0; v < kHalf; ++v) hrow[v] = fmaf(gl, hrow[v], dh[v]);
+      tmem_st32(trow + ST_H, hrow);
+      tmem_st_wait();
+      store_half_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, r, ch * 4, hrow);
     }
-    ra = nra;
-    rb = nrb;
+    SPHASE(9);  // H update
   }
 
   if (ok) {
-    tmem_ld64(trow + ST_H, hrow);
+    tmem_ld32w(trow + ST_H, hrow);
 #pragma unroll
-    for (int v = 0; v < kVT; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
+    for (int v = 0; v < kHalf; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
   } else if (t == 0 && p.status) {
     atomicExch(p.status, 1);
   }
@@ -493,9 +571,22 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   if (p.T > 0) {
     prep_kernel<<<static_cast<unsigned>(cap * p.HV), 128, kPrepSmem, stream>>>(p, maps, offs, a2);
   }
-  scan_kernel<<<static_cast<unsigned>(p.N * p.HV * kTiles), 128, kScanSmem, stream>>>(p, maps,
+  scan_kernel<<<static_cast<unsigned>(p.N * p.HV * kTiles), kScanThreads, kScanSmem, stream>>>(p, maps,
                                                                                      offs, a2);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace gdn
+
+#ifdef GDN_PHASE_PROFILE
+extern "C" __attribute__((visibility("default"))) int gdn_debug_scan_cycles(long long* host,
+                                                                              int reset) {
+  if (cudaMemcpyFromSymbol(host, gdn::g_scan_cycles, sizeof(long long) * 16) != cudaSuccess)
+    return -1;
+  if (reset) {
+    long long z[16] = {0};
+    if (cudaMemcpyToSymbol(gdn::g_scan_cycles, z, sizeof(z)) != cudaSuccess) return -1;
+  }
+  return 0;
+}
+#endif
