@@ -94,3 +94,18 @@ def test_chunked_status_word_clean():
     prefill.kernel(*x.args())
     torch.cuda.synchronize()
     assert prefill.device_status() == 0
+
+
+def test_partitioned_prefill_reassembles_to_full_call():
+    """A 4-rank plan (heads split: 3 sequences < 4 ranks) executed rank by rank on one
+    GPU through the partitioner's local packing equals one full call."""
+    from flashinfer_bench_tma_thrust_b200 import partition as PT
+    x = W.prefill_inputs([300, 0, 77], seed=41)
+    xd = to_dev(x)
+    ref_out, ref_state = prefill.kernel(*xd.args())
+    plan = PT.plan_prefill(x.lengths, 4, 16, 32)
+    assert plan.groups > 1
+    parts = [PT.run_prefill_local(plan, r, prefill.kernel, *xd.args()) for r in range(4)]
+    out, state = PT.assemble_prefill(parts, x.q.shape[0], 3, 32, x.cu_seqlens)
+    assert_out_close(out, ref_out, "partitioned vs full")
+    assert_state_close(state, ref_state, PREFILL_STATE_ATOL, "partitioned vs full")
