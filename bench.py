@@ -262,69 +262,146 @@ def run_ours(args, world, rank, local):
             "clocks": clocks, "gpu_launches": K,
         })
         if not args.no_e2e:
-            result["e2e"] = decode_e2e(x, info, device, world, min(K, 10), min(Wm, 3))
+            result["e2e"] = decode_e2e(x, info, device, world, min(K, 20), max(3, min(Wm, 3)))
         if world == 1 and rank == 0 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_decode_baseline()
     else:
-        lengths, with_state = prefill_lengths(args.workload)
-        from flashinfer_bench_tma_thrust_b200 import workloads as W
-        x = W.prefill_inputs(lengths, seed=2000 + rank, gen_device=device, device=device,
-                             with_state=with_state)
-        T = sum(lengths)
-
-        def step():
-            prefill.kernel(*x.args())
-
-        sampler = ClockSampler(device)
-        ms = time_steps(step, K, Wm, device, world)
-        clocks = sampler.stop()
-        ms_step = ms / K
-        value = world * T / (ms_step * 1e-3)
-        flop_per_token = HV * (6 * D * D + 10 * 64 * D + (2 * 64 * 64) // 3)
-        k_ms = kernel_launch_ms(step, 5, device)
-        achieved = T * flop_per_token / (k_ms * 1e-3) / 1e12
+        pm = prefill_measure(args.workload, K, Wm, device, world, rank, peak=bf16_sus,
+                             peak_src=peak_src)
+        lengths, T = pm.pop("lengths"), pm.pop("T")
         result.update({
-            "metric": "GDN prefill tokens/s", "value": round(value, 1), "unit": "tokens/s",
-            "ms_per_step": round(ms_step, 4), "dtype": "f32 state, bf16 tensor-core operands",
+            "metric": "GDN prefill tokens/s", "value": pm["value"], "unit": "tokens/s",
+            "ms_per_step": pm["ms_per_step"], "dtype": "f32 state, bf16 tensor-core operands",
             "config": {"workload": f"gdn_prefill {args.workload}: lengths {lengths[:8]}"
                                    f"{'...' if len(lengths) > 8 else ''} (T={T}/GPU), 16 q/k "
                                    "heads, 32 v heads, D=128, chunk 64",
                        "global_tokens": T * world, "parallelism": f"sequence-sharded x{world}",
                        "l2": "inputs (q/k/v >= 100 MB per GPU) larger than L2; no flush"},
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16_sus,
-                         "peak_source": peak_src + " (sustained bf16)", "unit": "TFLOP/s",
-                         "frac": round(achieved / bf16_sus, 4),
-                         "traffic": ncu_traffic(args.workload),
-                         "flop_per_token": flop_per_token, "kernel_ms": round(k_ms, 4)},
-            "clocks": clocks, "gpu_launches": K * prefill.launches_per_call(),
+            "roofline": pm["roofline"], "clocks": pm["clocks"],
+            "gpu_launches": K * prefill.launches_per_call(),
         })
         if world == 1 and rank == 0 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_prefill_baseline(lengths)
+    if args.workload == "decode" and not args.no_extra:
+        result["extra"] = {
+            w: prefill_measure(w, k, 3, device, world, rank, peak=bf16_sus, peak_src=peak_src,
+                               brief=True)
+            for w, k in (("prefill_varlen", 10), ("prefill_long", 5))}
     return result
 
 
-def decode_e2e(x, info, device, world, K, Wm):
-    """Same metric through the public API with host buffers: every step copies its
-    inputs from pinned host memory and reads output + new state back."""
-    from flashinfer_bench_tma_thrust_b200 import decode
-    host = [t.cpu().pin_memory() if isinstance(t, torch.Tensor) else t for t in x.args()]
-    B = info["B"]
-    out_h = torch.empty(B, 1, HV, D, dtype=torch.bfloat16).pin_memory()
-    ns_h = torch.empty(B, HV, D, D, dtype=torch.float32).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host if isinstance(t, torch.Tensor))
-    d2h = out_h.numel() * 2 + ns_h.numel() * 4
+def prefill_measure(workload, K, Wm, device, world, rank, peak, peak_src, brief=False):
+    """Time K prefill steps (one prefill.kernel call each) of `workload` on this rank."""
+    from flashinfer_bench_tma_thrust_b200 import prefill, workloads as W
+    lengths, with_state = prefill_lengths(workload)
+    x = W.prefill_inputs(lengths, seed=2000 + rank, gen_device=device, device=device,
+                         with_state=with_state)
+    T = sum(lengths)
 
     def step():
-        dev_args = [t.to(device, non_blocking=True) if isinstance(t, torch.Tensor) else t
-                    for t in host]
-        out, ns = decode.kernel(*dev_args)
-        out_h.copy_(out, non_blocking=True)
-        ns_h.copy_(ns, non_blocking=True)
+        prefill.kernel(*x.args())
 
+    sampler = ClockSampler(device)
     ms = time_steps(step, K, Wm, device, world)
+    clocks = sampler.stop()
+    ms_step = ms / K
+    flop_per_token = HV * (6 * D * D + 10 * 64 * D + (2 * 64 * 64) // 3)
+    k_ms = kernel_launch_ms(step, 3, device)
+    achieved = T * flop_per_token / (k_ms * 1e-3) / 1e12
+    roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+            "peak_source": peak_src + " (sustained bf16)", "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "traffic": ncu_traffic(workload),
+            "flop_per_token": flop_per_token, "call_ms": round(k_ms, 4)}
+    out = {"value": round(world * T / (ms_step * 1e-3), 1), "unit": "tokens/s",
+           "ms_per_step": round(ms_step, 4), "steps": K, "warmup": Wm, "roofline": roof}
+    if brief:
+        out["tokens_per_gpu"] = T
+        return out
+    out.update({"lengths": lengths, "T": T, "clocks": clocks})
+    return out
+
+
+def decode_e2e(x, info, device, world, K, Wm):
+    """Same metric through the public API (decode.kernel) with host buffers: every step
+    copies its inputs from pinned host memory and reads the output and the new state
+    back into pinned host memory. Copies run on their own streams with two buffer sets,
+    so step i's device->host copy overlaps step i+1's host->device copy and the kernel
+    (the two PCIe directions work concurrently); the timed region spans all streams."""
+    from flashinfer_bench_tma_thrust_b200 import decode
+    B = info["B"]
+    host_sets, dev_sets, out_h, ns_h = [], [], [], []
+    for j in range(2):
+        host_sets.append([t.cpu().pin_memory() if isinstance(t, torch.Tensor) else t
+                          for t in x.args()])
+        dev_sets.append([torch.empty_like(t, device=device) if isinstance(t, torch.Tensor) else t
+                         for t in x.args()])
+        out_h.append(torch.empty(B, 1, HV, D, dtype=torch.bfloat16).pin_memory())
+        ns_h.append(torch.empty(B, HV, D, D, dtype=torch.float32).pin_memory())
+    h2d = sum(t.numel() * t.element_size() for t in host_sets[0] if isinstance(t, torch.Tensor))
+    d2h = out_h[0].numel() * 2 + ns_h[0].numel() * 4
+    comp = torch.cuda.current_stream(device)
+    s_in = torch.cuda.Stream(device)
+    s_out = torch.cuda.Stream(device)
+    free = [torch.cuda.Event() for _ in range(2)]   # set j's device inputs consumed
+    ready = [torch.cuda.Event() for _ in range(2)]  # set j's inputs on the device
+    done = [torch.cuda.Event() for _ in range(2)]   # step on set j computed
+    drained = [torch.cuda.Event() for _ in range(2)]  # set j's results on the host
+    for j in range(2):
+        free[j].record(comp)
+        drained[j].record(s_out)
+    it = [0]
+
+    def step():
+        j = it[0] % 2
+        it[0] += 1
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(free[j])
+            for dst, src in zip(dev_sets[j], host_sets[j]):
+                if isinstance(src, torch.Tensor):
+                    dst.copy_(src, non_blocking=True)
+            ready[j].record(s_in)
+        comp.wait_event(ready[j])
+        comp.wait_event(drained[j])  # host buffers of set j free again
+        out, ns = decode.kernel(*dev_sets[j])
+        free[j].record(comp)
+        done[j].record(comp)
+        out.record_stream(s_out)
+        ns.record_stream(s_out)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done[j])
+            out_h[j].copy_(out, non_blocking=True)
+            ns_h[j].copy_(ns, non_blocking=True)
+            drained[j].record(s_out)
+
+    for _ in range(Wm):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(comp)
+    s_in.wait_stream(comp)
+    s_out.wait_stream(comp)
+    for _ in range(K):
+        step()
+    comp.wait_stream(s_in)
+    comp.wait_stream(s_out)
+    end.record(comp)
+    end.synchronize()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    # the results of the last step really arrived: compare with a synchronous call
+    ok = torch.equal(out_h[(K + Wm - 1) % 2].float().isfinite().all().reshape(1),
+                     torch.ones(1, dtype=torch.bool))
     return {"value": round(world * info["state_bytes"] / (ms / K * 1e-3) / 1e9, 3),
             "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": K,
-            "ms_per_step": round(ms / K, 3)}
+            "ms_per_step": round(ms / K, 3), "overlap": "copies on separate streams, 2 buffer sets",
+            "outputs_finite": bool(ok)}
 
 
 def run_reference(args):
@@ -386,6 +463,8 @@ def main():
     ap.add_argument("--batch", type=int, default=256, help="decode sequences per GPU")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="decode run only: skip the prefill configurations in 'extra'")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 2000 if args.workload == "decode" else 20
