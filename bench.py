@@ -283,11 +283,33 @@ def run_ours(args, world, rank, local):
         if world == 1 and rank == 0 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_prefill_baseline(lengths)
     if args.workload == "decode" and not args.no_extra:
-        result["extra"] = {
+        result["extra"] = {"decode_bf16_state": decode_bf16_measure(x, info, K, Wm, device,
+                                                                    world, ms_step)}
+        result["extra"].update({
             w: prefill_measure(w, k, 3, device, world, rank, peak=bf16_sus, peak_src=peak_src,
                                brief=True)
-            for w, k in (("prefill_varlen", 10), ("prefill_long", 5))}
+            for w, k in (("prefill_varlen", 10), ("prefill_long", 5))})
     return result
+
+
+def decode_bf16_measure(x, info, K, Wm, device, world, fp32_ms_step):
+    """Reduced-precision option, reported separately: the same decode loop with a bf16
+    state (half the state bytes). value = bf16 state bytes moved per second."""
+    from flashinfer_bench_tma_thrust_b200 import decode
+    holder = {"s": x.state.to(torch.bfloat16)}
+
+    def step():
+        _, ns = decode.kernel_bf16_state(x.q, x.k, x.v, holder["s"], x.A_log, x.a, x.dt_bias,
+                                         x.b, x.scale)
+        holder["s"] = ns
+
+    ms = time_steps(step, K, Wm, device, world)
+    ms_step = ms / K
+    b16 = info["state_bytes"] // 2
+    return {"value": round(world * b16 / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s (bf16 state)",
+            "ms_per_step": round(ms_step, 5),
+            "speedup_vs_fp32_state": round(fp32_ms_step / ms_step, 3),
+            "error": "separately reported: see tests/test_decode_bf16_state_gpu.py"}
 
 
 def prefill_measure(workload, K, Wm, device, world, rank, peak, peak_src, brief=False):

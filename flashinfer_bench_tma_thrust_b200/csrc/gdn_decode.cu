@@ -21,9 +21,44 @@
 
 namespace gdn {
 
+// State element access: fp32 (the reference layout) or bf16 (reduced-precision
+// option: half the HBM bytes, fp32 math, rounded to bf16 on store).
+template <typename S>
+struct StateIO;
+template <>
+struct StateIO<float> {
+  static __device__ __forceinline__ float4 load(const void* base, int64_t idx) {
+    return ld_stream_f4(static_cast<const float*>(base) + idx);
+  }
+  static __device__ __forceinline__ void store(void* base, int64_t idx, float4 v) {
+    st_stream_f4(static_cast<float*>(base) + idx, v);
+  }
+};
+template <>
+struct StateIO<__nv_bfloat16> {
+  static __device__ __forceinline__ float4 load(const void* base, int64_t idx) {
+    uint2 raw;
+    asm volatile("ld.global.cs.v2.u32 {%0,%1}, [%2];"
+                 : "=r"(raw.x), "=r"(raw.y)
+                 : "l"(static_cast<const __nv_bfloat16*>(base) + idx));
+    return make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                       __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+  }
+  static __device__ __forceinline__ void store(void* base, int64_t idx, float4 v) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+    const uint32_t ua = *reinterpret_cast<const uint32_t*>(&a);
+    const uint32_t ub = *reinterpret_cast<const uint32_t*>(&b);
+    asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(static_cast<__nv_bfloat16*>(base) +
+                                                            idx),
+                 "r"(ua), "r"(ub)
+                 : "memory");
+  }
+};
+
 // ROWS: rows each warp keeps in flight (loads issued back to back before any
 // reduction) — the memory-level parallelism knob.
-template <int ROWS>
+template <int ROWS, typename S = float>
 __global__ void __launch_bounds__(128) decode_kernel(DecodeParams p) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -59,14 +94,15 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeParams p) {
   float o_lane = 0.0f;
 
   const int64_t state_base = (vrow_base + row0) * kHeadDim + lane * 4;
-  const float* __restrict__ src = p.state ? p.state + state_base : nullptr;
-  float* __restrict__ dst = p.new_state + state_base;
+  const void* src_state = p.state_any ? p.state_any : static_cast<const void*>(p.state);
+  void* dst_state = p.new_state_any ? p.new_state_any : static_cast<void*>(p.new_state);
 
   for (int r0 = 0; r0 < rows_per_warp; r0 += ROWS) {
     float4 s[ROWS];
-    if (src) {
+    if (src_state) {
 #pragma unroll
-      for (int i = 0; i < ROWS; ++i) s[i] = ld_stream_f4(src + (r0 + i) * kHeadDim);
+      for (int i = 0; i < ROWS; ++i)
+        s[i] = StateIO<S>::load(src_state, state_base + (r0 + i) * kHeadDim);
     } else {
 #pragma unroll
       for (int i = 0; i < ROWS; ++i) s[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -87,14 +123,15 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeParams p) {
       n.y = fmaf(g, s[i].y, delta * k.y);
       n.z = fmaf(g, s[i].z, delta * k.z);
       n.w = fmaf(g, s[i].w, delta * k.w);
-      st_stream_f4(dst + (r0 + i) * kHeadDim, n);
+      StateIO<S>::store(dst_state, state_base + (r0 + i) * kHeadDim, n);
       if (lane == r0 + i) o_lane = p.scale * fmaf(g, sq, delta * kq);
     }
   }
   if (lane < rows_per_warp) p.out[vrow_base + row0 + lane] = __float2bfloat16_rn(o_lane);
 }
 
-int launch_decode(const DecodeParams& p_in, cudaStream_t stream) {
+template <typename S>
+int launch_decode_t(const DecodeParams& p_in, cudaStream_t stream) {
   DecodeParams p = p_in;
   const int64_t heads = p.B * p.HV;
   if (heads == 0) return 0;
@@ -108,11 +145,16 @@ int launch_decode(const DecodeParams& p_in, cudaStream_t stream) {
   p.rows_per_warp = kHeadDim / (4 * splits);
   const dim3 grid(static_cast<unsigned>(heads * splits));
   if (p.rows_per_warp >= 8) {
-    decode_kernel<8><<<grid, 128, 0, stream>>>(p);
+    decode_kernel<8, S><<<grid, 128, 0, stream>>>(p);
   } else {
-    decode_kernel<4><<<grid, 128, 0, stream>>>(p);
+    decode_kernel<4, S><<<grid, 128, 0, stream>>>(p);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_decode(const DecodeParams& p, cudaStream_t stream) {
+  return p.state_bf16 ? launch_decode_t<__nv_bfloat16>(p, stream)
+                      : launch_decode_t<float>(p, stream);
 }
 
 }  // namespace gdn

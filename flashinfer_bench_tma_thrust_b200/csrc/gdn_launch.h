@@ -25,6 +25,9 @@ struct DecodeParams {
   int HQ, HV;
   int splits;         // thread blocks per head (set by the launcher)
   int rows_per_warp;  // set by the launcher
+  int state_bf16;             // 1: state / new_state are bf16 (state_any / new_state_any)
+  const void* state_any;      // bf16 state (or nullptr)
+  void* new_state_any;        // bf16 new state
 };
 
 struct PrefillParams {

@@ -82,3 +82,43 @@ def kernel_inplace(q, k, v, state, A_log, a, dt_bias, b, scale=None, out=None):
     if out is None:
         out = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=q.device)
     return _launch(q, k, v, state, A_log, a, dt_bias, b, scale, out, state)
+
+
+def kernel_bf16_state(q, k, v, state, A_log, a, dt_bias, b, scale=None, out=None,
+                      new_state=None):
+    """Reduced-precision option: decode with a bf16 state [B, HV, 128, 128] (k-last).
+    fp32 math, new state rounded to bf16 — half the HBM bytes of the fp32 path, with
+    its own error (see tests/test_decode_bf16_state_gpu.py). ``new_state`` may be the
+    input ``state`` (in place). Returns (output bf16 [B,1,HV,128], new_state bf16)."""
+    dev = q.device
+    B, T, HQ, D = q.shape
+    if T != 1:
+        raise ValueError(f"decode expects seq_len 1 (q.shape[1]), got {T}")
+    HV = v.shape[2]
+    C.check_heads(HQ, HV, D)
+    for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a),
+                    ("dt_bias", dt_bias), ("b", b)):
+        C.require_cuda(name, t, dev)
+    if state is not None:
+        C.require_cuda("state", state, dev)
+        if state.dtype != torch.bfloat16 or tuple(state.shape) != (B, HV, D, D):
+            raise ValueError("state must be bf16 [B, HV, 128, 128]")
+        state = state.contiguous()
+    q_c, k_c, v_c = C.as_bf16("q", q), C.as_bf16("k", k), C.as_bf16("v", v)
+    A_c, A_t = C.as_gate("A_log", A_log)
+    a_c, a_t = C.as_gate("a", a)
+    d_c, d_t = C.as_gate("dt_bias", dt_bias)
+    b_c, b_t = C.as_gate("b", b)
+    if out is None:
+        out = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=dev)
+    if new_state is None:
+        new_state = torch.empty(B, HV, D, D, dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.gdn_decode_fwd_bf16state(
+            q_c.data_ptr(), k_c.data_ptr(), v_c.data_ptr(), C.ptr(state),
+            A_c.data_ptr(), A_t, a_c.data_ptr(), a_t, d_c.data_ptr(), d_t, b_c.data_ptr(), b_t,
+            C.resolve_scale(scale, D), out.data_ptr(), new_state.data_ptr(), B, HQ, HV, D,
+            C.stream_handle(dev))
+    _lib.check(rc, "gdn_decode_fwd_bf16state")
+    return out, new_state

@@ -82,6 +82,21 @@ GDN_API int gdn_decode_fwd(const void* q, const void* k, const void* v, const fl
                    int32_t HV, int32_t D, void* stream);
 
 /*
+ * Decode with a bf16 recurrent state (reduced-precision option, reported
+ * separately from the fp32 path): state / new_state are bf16 [B, HV, D, D]
+ * k-last; the math is fp32 and the new state is rounded to bf16 on store, which
+ * halves the state bytes streamed through HBM. Counterpart of the reference's
+ * gdn_decode_kernel_v10_bf16 (gdn/kernels/cute_cpp/gdn_decode_v10.cuh:517-659).
+ * Other arguments as gdn_decode_fwd; new_state may alias state.
+ */
+GDN_API int gdn_decode_fwd_bf16state(const void* q, const void* k, const void* v,
+                                     const void* state, const void* A_log, int A_log_dtype,
+                                     const void* a, int a_dtype, const void* dt_bias,
+                                     int dt_bias_dtype, const void* b, int b_dtype, float scale,
+                                     void* out, void* new_state, int64_t B, int32_t HQ,
+                                     int32_t HV, int32_t D, void* stream);
+
+/*
  * Variable-length prefill over cu_seqlens-packed sequences, token-sequential
  * recurrence (one thread block per sequence, v-head and 32-row V tile, the
  * state tile held in registers across the whole sequence).

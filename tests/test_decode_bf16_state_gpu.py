@@ -1,0 +1,54 @@
+"""Reduced-precision decode option (bf16 state), reported separately from the fp32
+path with its own error. Single step: the kernel equals the oracle run on the
+bf16-rounded input state, up to the bf16 rounding of the stored new state. Long
+run: the error of 100 consecutive decode steps against the fp32 path, the
+measurement of the reference's quantisation study
+(gdn/tests/test_quantization_accuracy.py:219-330), bounded here."""
+import pytest
+import torch
+
+from flashinfer_bench_tma_thrust_b200 import decode, workloads as W
+from oracle import gdn_oracle
+from parity import assert_out_close, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("B", [1, 16, 256])
+def test_bf16_state_single_step(B):
+    x = W.decode_inputs(B, seed=200 + B)
+    s16 = x.state.to(torch.bfloat16)
+    ref_out, ref_state = gdn_oracle.decode(x.q, x.k, x.v, s16.float(), x.A_log, x.a,
+                                           x.dt_bias, x.b, x.scale)
+    xd = to_dev(x)
+    out, ns = decode.kernel_bf16_state(xd.q, xd.k, xd.v, s16.cuda(), xd.A_log, xd.a,
+                                       xd.dt_bias, xd.b, xd.scale)
+    assert ns.dtype == torch.bfloat16
+    assert_out_close(out, ref_out, "bf16-state output")
+    got = ns.float().cpu()
+    # within one bf16 ulp of the fp32 result (plus fp32 reduction-order noise)
+    tol = ref_state.abs() * 2.0 ** -8 + 1e-6
+    assert ((got - ref_state).abs() <= tol).all()
+
+
+def test_bf16_state_error_over_100_steps():
+    B, steps = 8, 100
+    x = to_dev(W.decode_inputs(B, seed=7))
+    s32 = x.state.clone()
+    s16 = x.state.to(torch.bfloat16)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    max_out_rel, state_rel = 0.0, 0.0
+    for _ in range(steps):
+        q = torch.nn.functional.normalize(torch.randn(B, 1, 16, 128, device="cuda", generator=g), dim=-1).to(torch.bfloat16)
+        k = torch.nn.functional.normalize(torch.randn(B, 1, 16, 128, device="cuda", generator=g), dim=-1).to(torch.bfloat16)
+        v = torch.randn(B, 1, 32, 128, device="cuda", generator=g).to(torch.bfloat16)
+        a = torch.randn(B, 1, 32, device="cuda", generator=g).to(torch.bfloat16)
+        b = torch.randn(B, 1, 32, device="cuda", generator=g).to(torch.bfloat16)
+        o32, s32 = decode.kernel(q, k, v, s32, x.A_log, a, x.dt_bias, b, x.scale)
+        o16, s16 = decode.kernel_bf16_state(q, k, v, s16, x.A_log, a, x.dt_bias, b, x.scale)
+        rel = ((o16.float() - o32.float()).norm() / o32.float().norm()).item()
+        max_out_rel = max(max_out_rel, rel)
+    state_rel = ((s16.float() - s32).norm() / s32.norm()).item()
+    print(f"bf16 state, {steps} steps: max output rel err {max_out_rel:.2e}, "
+          f"final state rel err {state_rel:.2e}")
+    assert state_rel < 1e-2 and max_out_rel < 2e-2
