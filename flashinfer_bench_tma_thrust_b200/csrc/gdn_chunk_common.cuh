@@ -51,11 +51,7 @@ __device__ __forceinline__ void store_row_split(uint8_t* hi, uint8_t* lo, uint32
     uint32_t h[4], l[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      __nv_bfloat16 h0, l0, h1, l1;
-      split_bf16(v[c * 8 + 2 * e], h0, l0);
-      split_bf16(v[c * 8 + 2 * e + 1], h1, l1);
-      h[e] = pack_bf16(h0, h1);
-      l[e] = pack_bf16(l0, l1);
+      split2(v[c * 8 + 2 * e], v[c * 8 + 2 * e + 1], h[e], l[e]);
     }
     const uint32_t off = sw128_chunk(row, c);
     *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -111,14 +107,27 @@ __device__ __forceinline__ uint64_t op_desc(const Operand& o, uint32_t base, int
   return desc_kmajor(base + (s >> 2) * o.khalf + (s & 3) * 32);
 }
 
+// Byte offset of K step s from step 0 (added to the start-address field, which
+// holds address >> 4 in its low 14 bits; shared addresses stay below 256 KB).
+__device__ __forceinline__ uint64_t op_step(const Operand& o, int s) {
+  const uint32_t off = o.mn ? s * o.kstep : (s >> 2) * o.khalf + (s & 3) * 32;
+  return static_cast<uint64_t>(off >> 4);
+}
+
 __device__ __forceinline__ void issue_gemm(uint32_t d, const Operand& a, const Operand& b,
                                            uint32_t idesc, int ksteps) {
-  int n = 0;
-  for (int s = 0; s < ksteps; ++s) mma_bf16(d, op_desc(a, a.hi, s), op_desc(b, b.hi, s), idesc, n++ > 0);
-  if (b.lo)
-    for (int s = 0; s < ksteps; ++s) mma_bf16(d, op_desc(a, a.hi, s), op_desc(b, b.lo, s), idesc, 1);
-  if (a.lo)
-    for (int s = 0; s < ksteps; ++s) mma_bf16(d, op_desc(a, a.lo, s), op_desc(b, b.hi, s), idesc, 1);
+  const uint64_t ah = op_desc(a, a.hi, 0), bh = op_desc(b, b.hi, 0);
+  const uint64_t al = a.lo ? op_desc(a, a.lo, 0) : 0, bl = b.lo ? op_desc(b, b.lo, 0) : 0;
+#pragma unroll
+  for (int s = 0; s < ksteps; ++s) mma_bf16(d, ah + op_step(a, s), bh + op_step(b, s), idesc, s > 0);
+  if (b.lo) {
+#pragma unroll
+    for (int s = 0; s < ksteps; ++s) mma_bf16(d, ah + op_step(a, s), bl + op_step(b, s), idesc, 1);
+  }
+  if (a.lo) {
+#pragma unroll
+    for (int s = 0; s < ksteps; ++s) mma_bf16(d, al + op_step(a, s), bh + op_step(b, s), idesc, 1);
+  }
 }
 
 // Gates of the chunk's tokens (threads 0..63 hold the raw a, b of token t) and the
@@ -333,11 +342,7 @@ __device__ __forceinline__ void solve_tb(float* sAf, float* sTf, const float* sB
       uint32_t hw[4], lw[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        __nv_bfloat16 h0, l0, h1, l1;
-        split_bf16(vals[c * 8 + 2 * e], h0, l0);
-        split_bf16(vals[c * 8 + 2 * e + 1], h1, l1);
-        hw[e] = pack_bf16(h0, h1);
-        lw[e] = pack_bf16(l0, l1);
+        split2(vals[c * 8 + 2 * e], vals[c * 8 + 2 * e + 1], hw[e], lw[e]);
       }
       const uint32_t off = sw128_chunk(j, half * 4 + c);
       *reinterpret_cast<uint4*>(tb_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);

@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(128, 2)
             const int v0 = c * 8 + 2 * e;
             const float o0 = p.scale * fmaf(gam, qhv[v0], o[v0]);
             const float o1 = p.scale * fmaf(gam, qhv[v0 + 1], o[v0 + 1]);
-            w[e] = pack_bf16(__float2bfloat16_rn(o0), __float2bfloat16_rn(o1));
+            w[e] = pack2_rn(o0, o1);
           }
           *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
         }

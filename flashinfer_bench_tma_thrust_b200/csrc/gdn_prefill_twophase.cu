@@ -215,11 +215,7 @@ __global__ void __launch_bounds__(128, 3)
           uint32_t hw[4], lw[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            __nv_bfloat16 h0, l0, h1, l1;
-            split_bf16(r[c * 8 + 2 * e], h0, l0);
-            split_bf16(r[c * 8 + 2 * e + 1], h1, l1);
-            hw[e] = pack_bf16(h0, h1);
-            lw[e] = pack_bf16(l0, l1);
+            split2(r[c * 8 + 2 * e], r[c * 8 + 2 * e + 1], hw[e], lw[e]);
           }
           const uint32_t off = sw128_chunk(t, c);
           *reinterpret_cast<uint4*>(dst + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
@@ -252,7 +248,7 @@ constexpr uint32_t S_OFF_BETA = 98816;  // 2 x 64 fp32 (written by the gate scan
 constexpr uint32_t S_OFF_BAR = 99328;
 constexpr uint32_t kScanSmem = 99392 + 1024;
 constexpr uint32_t kScanTmemCols = 256;
-constexpr uint32_t ST_H = 0, ST_1 = 64, ST_2 = 128, ST_3 = 192;
+constexpr uint32_t ST_1 = 64, ST_2 = 128, ST_3 = 192;  // columns 0..63 unused
 constexpr int kScanThreads = 256;
 constexpr int kHalf = kVT / 2;  // columns per thread
 
@@ -265,11 +261,7 @@ __device__ __forceinline__ void store_half_row_split(uint8_t* hi, uint8_t* lo, u
     uint32_t hw[4], lw[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      __nv_bfloat16 h0, l0, h1, l1;
-      split_bf16(v[c * 8 + 2 * e], h0, l0);
-      split_bf16(v[c * 8 + 2 * e + 1], h1, l1);
-      hw[e] = pack_bf16(h0, h1);
-      lw[e] = pack_bf16(l0, l1);
+      split2(v[c * 8 + 2 * e], v[c * 8 + 2 * e + 1], hw[e], lw[e]);
     }
     const uint32_t off = sw128_chunk(row, c0 + c);
     *reinterpret_cast<uint4*>(hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
@@ -354,8 +346,6 @@ __global__ void __launch_bounds__(kScanThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + col0;
-  tmem_st32(trow + ST_H, hrow);
-  tmem_st_wait();
   store_half_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, r, ch * 4, hrow);
 
   const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
@@ -499,7 +489,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
             const int v0 = q * 8 + 2 * e;
             const float o0 = p.scale * fmaf(gam, qhv[v0], o[v0]);
             const float o1 = p.scale * fmaf(gam, qhv[v0 + 1], o[v0 + 1]);
-            w[e] = pack_bf16(__float2bfloat16_rn(o0), __float2bfloat16_rn(o1));
+            w[e] = pack2_rn(o0, o1);
           }
           *reinterpret_cast<uint4*>(dst + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
         }
@@ -516,22 +506,18 @@ __global__ void __launch_bounds__(kScanThreads, 2)
     SPHASE(8);  // G3 wait
     if (t == 0 && next < end) issue_tma(next);
     {
+      // the fp32 state row stays in registers for the whole sequence
       float dh[32];
-      tmem_ld32(trow + ST_3, dh);
-      tmem_ld32(trow + ST_H, hrow);
-      tmem_ld_wait();
+      tmem_ld32w(trow + ST_3, dh);
       const float gl = ex2(g_last);
 #pragma unroll
       for (int v = 0; v < kHalf; ++v) hrow[v] = fmaf(gl, hrow[v], dh[v]);
-      tmem_st32(trow + ST_H, hrow);
-      tmem_st_wait();
       store_half_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, r, ch * 4, hrow);
     }
     SPHASE(9);  // H update
   }
 
   if (ok) {
-    tmem_ld32w(trow + ST_H, hrow);
 #pragma unroll
     for (int v = 0; v < kHalf; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
   } else if (t == 0 && p.status) {
