@@ -351,6 +351,116 @@ __device__ __forceinline__ void solve_tb(float* sAf, float* sTf, const float* sB
   }
 }
 
+
+// ------------------------------------------------------------ 256-thread variants
+// Thread t owns row r = t % 128 (its TMEM lane) and the 32 columns [32c, 32c+32)
+// of it, c = t / 128.
+
+// From S = [K;Q] K^T in TMEM (ts_row already points at this thread's lane and column
+// half): rows r < 64 write A row r (fp32) into sAf; rows r >= 64 write row r - 64 of M
+// as bf16 hi/lo K-major rows of the m_hi / m_lo tiles.
+template <class Lay>
+__device__ __forceinline__ void build_a_m_256(uint32_t ts_row, float* sAf, const float* sG,
+                                              const float* sBeta, uint8_t* m_hi, uint8_t* m_lo) {
+  const int t = threadIdx.x, r = t & 127, c0 = (t >> 7) * 32;
+  float srow[32];
+  tmem_ld32(ts_row, srow);
+  tmem_ld_wait();
+  if (r < kC) {
+    const float gi = sG[r], bi = sBeta[r];
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      float4 w;
+      const int jj = c0 + j;
+      w.x = (jj + 0 < r) ? bi * ex2(gi - sG[jj + 0]) * srow[j + 0] : 0.f;
+      w.y = (jj + 1 < r) ? bi * ex2(gi - sG[jj + 1]) * srow[j + 1] : 0.f;
+      w.z = (jj + 2 < r) ? bi * ex2(gi - sG[jj + 2]) * srow[j + 2] : 0.f;
+      w.w = (jj + 3 < r) ? bi * ex2(gi - sG[jj + 3]) * srow[j + 3] : 0.f;
+      *reinterpret_cast<float4*>(sAf + Lay::idx(r, jj)) = w;
+    }
+  } else {
+    const int i = r - kC;
+    const float gi = sG[i];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) srow[j] = (c0 + j <= i) ? ex2(gi - sG[c0 + j]) * srow[j] : 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) split2(srow[c * 8 + 2 * e], srow[c * 8 + 2 * e + 1], hw[e], lw[e]);
+      const uint32_t off = sw128_chunk(i, (c0 >> 3) + c);
+      *reinterpret_cast<uint4*>(m_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(m_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+  }
+}
+
+// solve_tb for 256 threads (8 warps): same blocked algorithm, the finishing
+// products of each distance spread over more threads.
+template <class Lay>
+__device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float* sBeta,
+                                             uint8_t* tb_hi, uint8_t* tb_lo) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  if (warp < 4 && lane < 16) {
+    const int b0 = warp * 16;
+    float tc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < i; ++j) s = fmaf(sAf[Lay::idx(b0 + i, b0 + j)], tc[j], s);
+      tc[i] = (i < lane) ? 0.f : ((i == lane) ? 1.f : -s);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) sTf[Lay::idx(b0 + i, b0 + lane)] = tc[i];
+  }
+  __syncthreads();
+  // distance 1: partials on warps 0..2, finish on warps 0..5 (two warps per block)
+  if (warp < 3) solve_partial<Lay>(sAf, sTf, warp + 1, warp, warp, warp, warp + 1, lane);
+  __syncthreads();
+  if (warp < 6) {
+    const int b = warp >> 1;
+    solve_finish<Lay, 1, 64>(sTf, b + 1, b, b, b + 1, 0, 0, 0, 0, t & 63);
+  }
+  __syncthreads();
+  // distance 2: blocks (2,0), (3,1), two partials each on warps 0..3; finish 4 warps each
+  if (warp < 4) {
+    const int b = warp >> 1, I = 2 + b, J = b, K = J + (warp & 1);
+    solve_partial<Lay>(sAf, sTf, I, K, J, J, (warp & 1) ? J + 1 : I, lane);
+  }
+  __syncthreads();
+  {
+    const int b = warp >> 2, I = 2 + b, J = b;
+    solve_finish<Lay, 2, 128>(sTf, I, J, J, I, J, J + 1, 0, 0, t & 127);
+  }
+  __syncthreads();
+  // distance 3: block (3,0), partials K = 0, 1, 2 on warps 0..2; finish by all
+  if (warp < 3) solve_partial<Lay>(sAf, sTf, 3, warp, 0, 0, warp == 0 ? 3 : warp, lane);
+  __syncthreads();
+  solve_finish<Lay, 3, 256>(sTf, 3, 0, 0, 3, 0, 1, 0, 2, t);
+  __syncthreads();
+  {
+    // T_b = T diag(beta), MN-major rows j x cols n: a quarter row (2 chunks) per thread
+    const int j = t & (kC - 1), qq = t >> 6;
+    float vals[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const int nn = qq * 16 + c;
+      const bool lower = (nn >> 4) < (j >> 4) || ((nn >> 4) == (j >> 4) && nn <= j);
+      vals[c] = lower ? sTf[Lay::idx(j, nn)] * sBeta[nn] : 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) split2(vals[c * 8 + 2 * e], vals[c * 8 + 2 * e + 1], hw[e], lw[e]);
+      const uint32_t off = sw128_chunk(j, qq * 2 + c);
+      *reinterpret_cast<uint4*>(tb_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(tb_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+  }
+}
+
 struct ChunkTmaps {
   CUtensorMap k;  // [T, HQ, 128] bf16: dims {128, HQ, T}, box {64, 1, 64}, 128B swizzle
   CUtensorMap q;

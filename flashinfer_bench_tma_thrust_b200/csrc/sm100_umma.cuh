@@ -89,14 +89,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// One poll; the thread may sleep up to kSuspendHintNs inside it (woken as soon as
+// the phase completes), so waiting warps do not spin on the issue slots.
+constexpr uint32_t kSuspendHintNs = 100000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(addr), "r"(parity)
+      : "r"(addr), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return done != 0;
 }
@@ -110,7 +113,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1; i < kSpinLimit; ++i) {
     if (mbar_try_wait(addr, parity)) return true;
-    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if ((i & 7u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
   return false;
 }
