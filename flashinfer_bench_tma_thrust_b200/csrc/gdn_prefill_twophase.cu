@@ -104,24 +104,27 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
 }
 
 // ------------------------------------------------------------------ prep
-// Shared memory: KQ tile (32 KB, TMA) — dead after S, then the fp32 A and T of the
-// solve (padded rows, 17 KB each; T spills 2 KB past the tile), then T_b hi/lo over
-// A; [I; M] hi/lo (32 KB).
+// 256 threads; thread t owns TMEM lane / row t % 128 and a 32-column half of it.
+// Shared memory: the K/Q tile (32 KB, TMA) is dead after S and then holds the fp32 A
+// and T of the solve (padded rows, 17 KB each), then T_b hi/lo over A. M hi/lo (rows
+// 0..63 of the A operand of P = M T_b; the operand's rows 64..127 read whatever
+// follows — those result rows are not used).
 constexpr uint32_t P_OFF_KQ = 0;
 constexpr uint32_t P_OFF_AF = 0;
 constexpr uint32_t P_OFF_TF = 17408;
 constexpr uint32_t P_OFF_TB_HI = 0;
 constexpr uint32_t P_OFF_TB_LO = 8192;
-constexpr uint32_t P_OFF_A2_HI = 35840;   // 1024-aligned, after T
-constexpr uint32_t P_OFF_A2_LO = 52224;
-constexpr uint32_t P_OFF_G = 68608;
-constexpr uint32_t P_OFF_BETA = 68864;
-constexpr uint32_t P_OFF_BAR = 69120;
-constexpr uint32_t kPrepSmem = 69184 + 1024;
+constexpr uint32_t P_OFF_M_HI = 35840;   // 1024-aligned, after T
+constexpr uint32_t P_OFF_M_LO = 44032;   // rows 64..127 of the hi operand = these rows
+constexpr uint32_t P_OFF_G = 60416;      // (52224..60416: rows 64..127 of the lo operand)
+constexpr uint32_t P_OFF_BETA = 60672;
+constexpr uint32_t P_OFF_BAR = 60928;
+constexpr uint32_t kPrepSmem = 60992 + 1024;
 constexpr uint32_t kPrepTmemCols = 128;
 constexpr uint32_t PT_S = 0, PT_P = 64;
+constexpr int kPrepThreads = 256;
 
-__global__ void __launch_bounds__(128, 3)
+__global__ void __launch_bounds__(kPrepThreads, 2)
     prep_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
                 const int64_t* __restrict__ offs, uint8_t* __restrict__ a2_out) {
   extern __shared__ uint8_t smem_raw[];
@@ -135,7 +138,7 @@ __global__ void __launch_bounds__(128, 3)
   uint64_t* bar_mma = bar_tma + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P_OFF_BAR + 16);
 
-  const int t = threadIdx.x, warp = t >> 5;
+  const int t = threadIdx.x, warp = t >> 5, r = t & 127, c0 = (t >> 7) * 32;
   const int h = static_cast<int>(blockIdx.x % p.HV);
   const int64_t gchunk = blockIdx.x / p.HV;
   const int64_t total = offs[p.N];
@@ -177,7 +180,7 @@ __global__ void __launch_bounds__(128, 3)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + c0;
 
   chunk_gates(ra, rb, L, A_log, dtb, sG, sBeta);
   bool ok = mbar_wait(bar_tma, 0);
@@ -192,35 +195,44 @@ __global__ void __launch_bounds__(128, 3)
     tc_fence_after();
     if (__syncthreads_and(ok)) {
       // the K/Q tile is dead: A, T and T_b reuse its space
-      build_a_m<PadLayout>(trow + PT_S, sAf, sG, sBeta, sm + P_OFF_A2_HI, sm + P_OFF_A2_LO);
+      build_a_m_256<PadLayout>(trow + PT_S, sAf, sG, sBeta, sm + P_OFF_M_HI, sm + P_OFF_M_LO);
       __syncthreads();
-      solve_tb<PadLayout>(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
+      solve_tb_256<PadLayout>(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
       sync_before_mma();
-      if (t == 0) {
-        const Operand a2{smem_u32(sm + P_OFF_A2_HI), smem_u32(sm + P_OFF_A2_LO), false, 0, 0, 0};
+      if (t == 0) {  // P = M T_b (result rows 0..63)
+        const Operand mA{smem_u32(sm + P_OFF_M_HI), smem_u32(sm + P_OFF_M_LO), false, 0, 0, 0};
         const Operand tb{smem_u32(sm + P_OFF_TB_HI), smem_u32(sm + P_OFF_TB_LO), true, 8192,
                          2048, 0};
-        issue_gemm(tmem + PT_P, a2, tb, ID_KM, 4);
+        issue_gemm(tmem + PT_P, mA, tb, ID_KM, 4);
         mma_commit(bar_mma);
+      }
+      // meanwhile: the T_b rows of [T_b; P] are the T_b tiles themselves (same swizzled
+      // row image): copy hi to rows 0..63 of the hi part, lo to the lo part
+      uint8_t* dst = a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) * kA2Bytes;
+      {
+        const uint4* src_hi = reinterpret_cast<const uint4*>(sm + P_OFF_TB_HI);
+        const uint4* src_lo = reinterpret_cast<const uint4*>(sm + P_OFF_TB_LO);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int idx = t + q * kPrepThreads;  // 512 x 16 B = 8 KB per tile
+          reinterpret_cast<uint4*>(dst)[idx] = src_hi[idx];
+          reinterpret_cast<uint4*>(dst + 16384)[idx] = src_lo[idx];
+        }
       }
       ok = mbar_wait(bar_mma, 1);
       tc_fence_after();
-      if (__syncthreads_and(ok)) {
-        // row t of [T_b; P] -> hi (all rows) and lo (rows 0..63) swizzled image in HBM
-        float r[64];
-        tmem_ld64(trow + PT_P, r);
-        uint8_t* dst = a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) * kA2Bytes;
+      if (__syncthreads_and(ok) && r < kC) {
+        // row r of P -> hi only (P only reaches the bf16 output), rows 64..127 of the hi part
+        float pr[32];
+        tmem_ld32(trow + PT_P, pr);
+        tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t hw[4], lw[4];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t w[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            split2(r[c * 8 + 2 * e], r[c * 8 + 2 * e + 1], hw[e], lw[e]);
-          }
-          const uint32_t off = sw128_chunk(t, c);
-          *reinterpret_cast<uint4*>(dst + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          if (t < kC)
-            *reinterpret_cast<uint4*>(dst + 16384 + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          for (int e = 0; e < 4; ++e) w[e] = pack2_rn(pr[c * 8 + 2 * e], pr[c * 8 + 2 * e + 1]);
+          *reinterpret_cast<uint4*>(dst + 8192 + sw128_chunk(r, (c0 >> 3) + c)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
     }
@@ -555,7 +567,7 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   chunk_offsets_kernel<<<1, 1024, 0, stream>>>(p, offs);
   const int64_t cap = (p.T + kC - 1) / kC + p.N;
   if (p.T > 0) {
-    prep_kernel<<<static_cast<unsigned>(cap * p.HV), 128, kPrepSmem, stream>>>(p, maps, offs, a2);
+    prep_kernel<<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(p, maps, offs, a2);
   }
   scan_kernel<<<static_cast<unsigned>(p.N * p.HV * kTiles), kScanThreads, kScanSmem, stream>>>(p, maps,
                                                                                      offs, a2);
