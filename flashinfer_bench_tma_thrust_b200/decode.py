@@ -122,3 +122,24 @@ def kernel_bf16_state(q, k, v, state, A_log, a, dt_bias, b, scale=None, out=None
             C.stream_handle(dev))
     _lib.check(rc, "gdn_decode_fwd_bf16state")
     return out, new_state
+
+
+def kernel_multitoken(q, k, v, state, A_log, a, dt_bias, b, scale=None):
+    """Decode T >= 1 tokens per sequence in one call (speculative / multi-token decode).
+
+    Shapes as ``kernel`` with T = q.shape[1] tokens per sequence: q, k [B,T,HQ,128],
+    v [B,T,HV,128], a, b [B,T,HV]. The B sequences are equal-length segments of one
+    chunked prefill (cu_seqlens = 0, T, 2T, ...), so the result is the same as T
+    consecutive ``kernel`` calls. Returns (output [B,T,HV,128] bf16, new_state fp32).
+    """
+    from . import prefill
+    B, T, HQ, D = q.shape
+    HV = v.shape[2]
+    if T == 1:
+        return kernel(q, k, v, state, A_log, a, dt_bias, b, scale)
+    cu = torch.arange(0, (B + 1) * T, T, dtype=torch.int64, device=q.device)
+    out, new_state = prefill.kernel(q.reshape(B * T, HQ, D), k.reshape(B * T, HQ, D),
+                                    v.reshape(B * T, HV, D), state, A_log,
+                                    a.reshape(B * T, HV), dt_bias, b.reshape(B * T, HV), cu,
+                                    scale)
+    return out.view(B, T, HV, D), new_state

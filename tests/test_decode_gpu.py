@@ -117,3 +117,29 @@ def test_decode_rejects_bad_inputs():
         decode.kernel(x.q.cpu(), x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.scale)
     with pytest.raises(TypeError):
         decode.kernel(x.q.float(), x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.scale)
+
+
+@pytest.mark.parametrize("T", [2, 7, 65])
+def test_multitoken_decode_equals_consecutive_steps(T):
+    """T tokens per sequence in one call == T single-token decode steps (oracle)."""
+    B = 3
+    g = torch.Generator().manual_seed(T)
+    x = W.decode_inputs(B, seed=T)
+    q = torch.nn.functional.normalize(torch.randn(B, T, 16, 128, generator=g), dim=-1).to(torch.bfloat16)
+    k = torch.nn.functional.normalize(torch.randn(B, T, 16, 128, generator=g), dim=-1).to(torch.bfloat16)
+    v = torch.randn(B, T, 32, 128, generator=g).to(torch.bfloat16)
+    a = torch.randn(B, T, 32, generator=g).to(torch.bfloat16)
+    b = torch.randn(B, T, 32, generator=g).to(torch.bfloat16)
+    s = x.state
+    ref_outs = []
+    for t in range(T):
+        o, s = gdn_oracle.decode(q[:, t:t + 1], k[:, t:t + 1], v[:, t:t + 1], s, x.A_log,
+                                 a[:, t:t + 1], x.dt_bias, b[:, t:t + 1], x.scale)
+        ref_outs.append(o)
+    ref_out = torch.cat(ref_outs, dim=1)
+    dv = lambda t: t.cuda()  # noqa: E731
+    out, ns = decode.kernel_multitoken(dv(q), dv(k), dv(v), dv(x.state), dv(x.A_log), dv(a),
+                                       dv(x.dt_bias), dv(b), x.scale)
+    assert out.shape == (B, T, 32, 128)
+    assert_out_close(out, ref_out, f"T={T}")
+    assert_state_close(ns, s, DECODE_STATE_ATOL * 5, f"T={T}")
