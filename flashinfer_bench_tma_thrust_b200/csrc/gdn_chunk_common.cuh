@@ -164,8 +164,10 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
 // barrier so that the other warps can work meanwhile. Readers of sG / sBeta in
 // other warps must pass a block-wide barrier afterwards.
 __device__ __forceinline__ void chunk_gates_w01(float ra, float rb, int L, float A_log,
-                                                float dtb, float* sG, float* sBeta) {
-  const int t = threadIdx.x, lane = t & 31;
+                                                float dtb, float* sG, float* sBeta,
+                                                int base = 0) {
+  // the two warps are threads [base, base + 64); token index t = thread - base
+  const int t = threadIdx.x - base, lane = t & 31;
   const bool valid = t < L;
   const float lg = valid ? gate_log_decay(A_log, ra, dtb) * kLog2e : 0.0f;
   const float beta = valid ? gate_beta(rb) : 0.0f;

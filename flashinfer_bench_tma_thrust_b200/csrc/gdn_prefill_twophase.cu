@@ -262,6 +262,13 @@ constexpr uint32_t kScanSmem = 99392 + 1024;
 constexpr uint32_t kScanTmemCols = 256;
 constexpr uint32_t ST_1 = 64, ST_2 = 128, ST_3 = 192;  // columns 0..63 unused
 constexpr int kScanThreads = 256;
+// Thread that issues the MMAs, TMA and bulk copies: warp 3 (rows 96..127), whose own
+// per-chunk work (output rows) is off the state chain, so the cycles it spends
+// blocked on MMA issue do not delay the chain's conversions.
+constexpr int kIssuer = 96;
+// Warps 4-5 (threads 128..191, idle while the state-update MMA runs) load the raw
+// gates and compute the next chunk's decays.
+constexpr int kGateBase = 128;
 constexpr int kHalf = kVT / 2;  // columns per thread
 
 // Split 32 fp32 values into bf16 hi/lo and write them as chunks [c0, c0+4) of
@@ -363,8 +370,8 @@ __global__ void __launch_bounds__(kScanThreads, 2)
   const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
   const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
   auto load_gates = [&](int64_t cs, float& ra, float& rb) {
-    if (t < kC) {
-      const int64_t tok = cs + t;
+    if (t >= kGateBase && t < kGateBase + kC) {
+      const int64_t tok = cs + (t - kGateBase);
       const bool valid = tok < end;
       ra = valid ? load_scalar(p.a, p.a_dtype, tok * HV + h) : 0.0f;
       rb = valid ? load_scalar(p.b, p.b_dtype, tok * HV + h) : 0.0f;
@@ -374,13 +381,15 @@ __global__ void __launch_bounds__(kScanThreads, 2)
   uint32_t tma_phase = 0, a2_phase = 0, mma_phase = 0;
   bool ok = true;
   float ra = 0.f, rb = 0.f;
-  if (t == 0) {
+  if (t == kIssuer) {
     issue_tma(start);
     issue_a2(0);
   }
   load_gates(start, ra, rb);
-  chunk_gates(ra, rb, static_cast<int>((end - start) < kC ? (end - start) : kC), A_log, dtb,
-              sG0, sBeta0);
+  if (t >= kGateBase && t < kGateBase + kC)
+    chunk_gates_w01(ra, rb, static_cast<int>((end - start) < kC ? (end - start) : kC), A_log,
+                    dtb, sG0, sBeta0, kGateBase);
+  __syncthreads();
 
   int64_t c = 0;
 #ifdef GDN_PHASE_PROFILE
@@ -399,7 +408,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
     SPHASE(1);  // TMA wait
     sync_before_mma();
     if (!__syncthreads_and(ok)) break;
-    if (t == 0) {
+    if (t == kIssuer) {
       const Operand kq{smem_u32(sm + S_OFF_KQ), 0, false, 0, 0, 16384};
       const Operand hB{smem_u32(sm + S_OFF_H_HI), smem_u32(sm + S_OFF_H_LO), true, 8192, 2048, 0};
       issue_gemm(tmem + ST_1, kq, hB, ID_KM, 8);
@@ -450,7 +459,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
     SPHASE(4);  // A2 wait
     sync_before_mma();
     if (!__syncthreads_and(ok)) break;
-    if (t == 0) {
+    if (t == kIssuer) {
       const Operand a2{smem_u32(sm + S_OFF_A2_HI), smem_u32(sm + S_OFF_A2_LO), false, 0, 0, 0};
       const Operand xb{smem_u32(sm + S_OFF_X_HI), smem_u32(sm + S_OFF_X_LO), true, 8192, 2048, 0};
       issue_gemm(tmem + ST_2, a2, xb, ID_KM, 4);
@@ -461,7 +470,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
-    if (t == 0 && next < end) issue_a2(c + 1);  // [T_b; P] of this chunk is consumed
+    if (t == kIssuer && next < end) issue_a2(c + 1);  // [T_b; P] of this chunk is consumed
     if (r < kC) {
       // f_j U_j with f_j = e^{Gamma_last - Gamma_j} (0 for padded rows): the state
       // update then reads the raw K tile, dH = K^T diag(f) U
@@ -476,7 +485,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
 
     // ---- dH = K^T diag(f) U (into its own TMEM columns, so O' stays readable) -------------
     sync_before_mma();
-    if (t == 0) {
+    if (t == kIssuer) {
       const Operand kt{smem_u32(sm + S_OFF_KQ), 0, true, 16384, 2048, 0};
       const Operand ub{smem_u32(sm + S_OFF_X_HI), smem_u32(sm + S_OFF_X_LO), true, 8192, 2048, 0};
       issue_gemm(tmem + ST_3, kt, ub, ID_MM, 4);
@@ -506,9 +515,10 @@ __global__ void __launch_bounds__(kScanThreads, 2)
           *reinterpret_cast<uint4*>(dst + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-    } else if (t < kC && next < end) {
+    } else if (t >= kGateBase && t < kGateBase + kC && next < end) {
       const int nL = static_cast<int>((end - next) < kC ? (end - next) : kC);
-      chunk_gates_w01(nra, nrb, nL, A_log, dtb, sG0 + (buf ^ 1) * kC, sBeta0 + (buf ^ 1) * kC);
+      chunk_gates_w01(nra, nrb, nL, A_log, dtb, sG0 + (buf ^ 1) * kC, sBeta0 + (buf ^ 1) * kC,
+                      kGateBase);
     }
     SPHASE(7);  // G3 issue + O + next gates
     ok = mbar_wait(bar_mma, mma_phase);
@@ -516,7 +526,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
     SPHASE(8);  // G3 wait
-    if (t == 0 && next < end) issue_tma(next);
+    if (t == kIssuer && next < end) issue_tma(next);
     {
       // the fp32 state row stays in registers for the whole sequence
       float dh[32];
@@ -532,7 +542,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
   if (ok) {
 #pragma unroll
     for (int v = 0; v < kHalf; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
-  } else if (t == 0 && p.status) {
+  } else if (t == kIssuer && p.status) {
     atomicExch(p.status, 1);
   }
   tc_fence_before();
