@@ -124,7 +124,7 @@ constexpr uint32_t kPrepTmemCols = 128;
 constexpr uint32_t PT_S = 0, PT_P = 64;
 constexpr int kPrepThreads = 256;
 
-__global__ void __launch_bounds__(kPrepThreads, 2)
+__global__ void __launch_bounds__(kPrepThreads, 3)
     prep_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
                 const int64_t* __restrict__ offs, uint8_t* __restrict__ a2_out) {
   extern __shared__ uint8_t smem_raw[];
