@@ -397,59 +397,90 @@ __device__ __forceinline__ void build_a_m_256(uint32_t ts_row, float* sAf, const
   }
 }
 
-// solve_tb for 256 threads (8 warps): same blocked algorithm, the finishing
-// products of each distance spread over more threads.
+// solve_tb for 256 threads (8 warps), written for instruction count (the prep
+// kernel runs three blocks per SM and is issue-bound): diagonal blocks by
+// right-looking substitution (each step's updates are independent), off-diagonal
+// blocks one warp per block with 8 outputs per lane and float4 loads.
 template <class Lay>
 __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float* sBeta,
                                              uint8_t* tb_hi, uint8_t* tb_lo) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   if (warp < 4 && lane < 16) {
+    // column `lane` of the inverse of the unit lower block b0: x_i = d_i - sum_{j<i} A_ij x_j
     const int b0 = warp * 16;
-    float tc[16];
+    float x[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float s = 0.f;
+    for (int i = 0; i < 16; ++i) x[i] = (i == lane) ? 1.f : 0.f;
 #pragma unroll
-      for (int j = 0; j < i; ++j) s = fmaf(sAf[Lay::idx(b0 + i, b0 + j)], tc[j], s);
-      tc[i] = (i < lane) ? 0.f : ((i == lane) ? 1.f : -s);
+    for (int j = 0; j < 15; ++j) {
+#pragma unroll
+      for (int i = j + 1; i < 16; ++i) x[i] = fmaf(-sAf[Lay::idx(b0 + i, b0 + j)], x[j], x[i]);
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) sTf[Lay::idx(b0 + i, b0 + lane)] = tc[i];
+    for (int i = 0; i < 16; ++i) sTf[Lay::idx(b0 + i, b0 + lane)] = x[i];
   }
   __syncthreads();
-  // distance 1: partials on warps 0..2, finish on warps 0..5 (two warps per block)
-  if (warp < 3) solve_partial<Lay>(sAf, sTf, warp + 1, warp, warp, warp, warp + 1, lane);
-  __syncthreads();
-  if (warp < 6) {
-    const int b = warp >> 1;
-    solve_finish<Lay, 1, 64>(sTf, b + 1, b, b, b + 1, 0, 0, 0, 0, t & 63);
+  const int r = lane >> 1, c0 = (lane & 1) * 8;
+  for (int d = 1; d < 4; ++d) {
+    if (warp < 4 - d) {
+      const int I = d + warp, J = warp;
+      float w[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e] = 0.f;
+      for (int K = J; K < I; ++K) {  // W_IJ = sum_K A_IK T_KJ
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float a = sAf[Lay::idx(16 * I + r, 16 * K + k)];
+          const float4 t0 = *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * K + k, 16 * J + c0));
+          const float4 t1 =
+              *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * K + k, 16 * J + c0 + 4));
+          w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
+          w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
+          w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
+          w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
+        }
+      }
+      // scratch block (J, I)
+      *reinterpret_cast<float4*>(sTf + Lay::idx(16 * J + r, 16 * I + c0)) =
+          make_float4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<float4*>(sTf + Lay::idx(16 * J + r, 16 * I + c0 + 4)) =
+          make_float4(w[4], w[5], w[6], w[7]);
+      __syncwarp();
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {  // T_IJ = -T_II W_IJ
+        const float a = sTf[Lay::idx(16 * I + r, 16 * I + k)];
+        const float4 t0 = *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * J + k, 16 * I + c0));
+        const float4 t1 =
+            *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * J + k, 16 * I + c0 + 4));
+        w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
+        w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
+        w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
+        w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
+      }
+      *reinterpret_cast<float4*>(sTf + Lay::idx(16 * I + r, 16 * J + c0)) =
+          make_float4(-w[0], -w[1], -w[2], -w[3]);
+      *reinterpret_cast<float4*>(sTf + Lay::idx(16 * I + r, 16 * J + c0 + 4)) =
+          make_float4(-w[4], -w[5], -w[6], -w[7]);
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  // distance 2: blocks (2,0), (3,1), two partials each on warps 0..3; finish 4 warps each
-  if (warp < 4) {
-    const int b = warp >> 1, I = 2 + b, J = b, K = J + (warp & 1);
-    solve_partial<Lay>(sAf, sTf, I, K, J, J, (warp & 1) ? J + 1 : I, lane);
-  }
-  __syncthreads();
-  {
-    const int b = warp >> 2, I = 2 + b, J = b;
-    solve_finish<Lay, 2, 128>(sTf, I, J, J, I, J, J + 1, 0, 0, t & 127);
-  }
-  __syncthreads();
-  // distance 3: block (3,0), partials K = 0, 1, 2 on warps 0..2; finish by all
-  if (warp < 3) solve_partial<Lay>(sAf, sTf, 3, warp, 0, 0, warp == 0 ? 3 : warp, lane);
-  __syncthreads();
-  solve_finish<Lay, 3, 256>(sTf, 3, 0, 0, 3, 0, 1, 0, 2, t);
-  __syncthreads();
   {
     // T_b = T diag(beta), MN-major rows j x cols n: a quarter row (2 chunks) per thread
     const int j = t & (kC - 1), qq = t >> 6;
     float vals[16];
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
+    for (int c = 0; c < 16; c += 4) {
       const int nn = qq * 16 + c;
-      const bool lower = (nn >> 4) < (j >> 4) || ((nn >> 4) == (j >> 4) && nn <= j);
-      vals[c] = lower ? sTf[Lay::idx(j, nn)] * sBeta[nn] : 0.f;
+      const float4 tv = *reinterpret_cast<const float4*>(sTf + Lay::idx(j, nn));
+      const float tvs[4] = {tv.x, tv.y, tv.z, tv.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int m = nn + e;
+        const bool lower = (m >> 4) < (j >> 4) || ((m >> 4) == (j >> 4) && m <= j);
+        vals[c + e] = lower ? tvs[e] * sBeta[m] : 0.f;
+      }
     }
 #pragma unroll
     for (int c = 0; c < 2; ++c) {

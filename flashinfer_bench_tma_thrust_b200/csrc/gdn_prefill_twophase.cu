@@ -43,10 +43,24 @@ __device__ long long g_scan_cycles[16];
       sphase_last_ = now_;                            \
     }                                                 \
   } while (0)
+__device__ long long g_prep_cycles[16];
+#define PPHASE(i)                                     \
+  do {                                                \
+    if (blockIdx.x == 0 && threadIdx.x == 0) {        \
+      const long long now_ = clock64();               \
+      g_prep_cycles[i] += now_ - pphase_last_;        \
+      pphase_last_ = now_;                            \
+    }                                                 \
+  } while (0)
+#define PPHASE_INIT long long pphase_last_ = clock64()
 #else
 #define SPHASE(i) \
   do {            \
   } while (0)
+#define PPHASE(i) \
+  do {            \
+  } while (0)
+#define PPHASE_INIT
 #endif  // per (chunk, v-head): hi 16 KB + lo rows 0..63 8 KB
 
 __device__ __forceinline__ void seq_bounds(const PrefillParams& p, int64_t n, int64_t& start,
@@ -182,8 +196,11 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
   const uint32_t tmem = *tmem_slot;
   const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + c0;
 
+  PPHASE_INIT;
   chunk_gates(ra, rb, L, A_log, dtb, sG, sBeta);
+  PPHASE(0);  // gates
   bool ok = mbar_wait(bar_tma, 0);
+  PPHASE(1);  // TMA wait
   sync_before_mma();
   if (__syncthreads_and(ok)) {
     if (t == 0) {
@@ -193,11 +210,14 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
     }
     ok = mbar_wait(bar_mma, 0);
     tc_fence_after();
+    PPHASE(2);  // S MMA
     if (__syncthreads_and(ok)) {
       // the K/Q tile is dead: A, T and T_b reuse its space
       build_a_m_256<PadLayout>(trow + PT_S, sAf, sG, sBeta, sm + P_OFF_M_HI, sm + P_OFF_M_LO);
       __syncthreads();
+      PPHASE(3);  // build A, M
       solve_tb_256<PadLayout>(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
+      PPHASE(4);  // solve + T_b
       sync_before_mma();
       if (t == 0) {  // P = M T_b (result rows 0..63)
         const Operand mA{smem_u32(sm + P_OFF_M_HI), smem_u32(sm + P_OFF_M_LO), false, 0, 0, 0};
@@ -219,8 +239,10 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
           reinterpret_cast<uint4*>(dst + 16384)[idx] = src_lo[idx];
         }
       }
+      PPHASE(5);  // P issue + T_b copy
       ok = mbar_wait(bar_mma, 1);
       tc_fence_after();
+      PPHASE(6);  // P wait
       if (__syncthreads_and(ok) && r < kC) {
         // row r of P -> hi only (P only reaches the bf16 output), rows 64..127 of the hi part
         float pr[32];
@@ -235,6 +257,7 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
               make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      PPHASE(7);  // P rows write
     }
   }
   if (!ok && t == 0 && p.status) atomicExch(p.status, 1);
@@ -587,6 +610,16 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
 }  // namespace gdn
 
 #ifdef GDN_PHASE_PROFILE
+extern "C" __attribute__((visibility("default"))) int gdn_debug_prep_cycles(long long* host,
+                                                                              int reset) {
+  if (cudaMemcpyFromSymbol(host, gdn::g_prep_cycles, sizeof(long long) * 16) != cudaSuccess)
+    return -1;
+  if (reset) {
+    long long z[16] = {0};
+    if (cudaMemcpyToSymbol(gdn::g_prep_cycles, z, sizeof(z)) != cudaSuccess) return -1;
+  }
+  return 0;
+}
 extern "C" __attribute__((visibility("default"))) int gdn_debug_scan_cycles(long long* host,
                                                                               int reset) {
   if (cudaMemcpyFromSymbol(host, gdn::g_scan_cycles, sizeof(long long) * 16) != cudaSuccess)
