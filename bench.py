@@ -284,7 +284,9 @@ def run_ours(args, world, rank, local):
             result["cpu_baseline"] = cpu_prefill_baseline(lengths)
     if args.workload == "decode" and not args.no_extra:
         result["extra"] = {"decode_bf16_state": decode_bf16_measure(x, info, K, Wm, device,
-                                                                    world, ms_step)}
+                                                                    world, ms_step),
+                           "decode_fp8_state": decode_fp8_measure(x, info, K, Wm, device,
+                                                                  world, ms_step)}
         result["extra"].update({
             w: prefill_measure(w, k, 3, device, world, rank, peak=bf16_sus, peak_src=peak_src,
                                brief=True)
@@ -310,6 +312,27 @@ def decode_bf16_measure(x, info, K, Wm, device, world, fp32_ms_step):
             "ms_per_step": round(ms_step, 5),
             "speedup_vs_fp32_state": round(fp32_ms_step / ms_step, 3),
             "error": "separately reported: see tests/test_decode_bf16_state_gpu.py"}
+
+
+def decode_fp8_measure(x, info, K, Wm, device, world, fp32_ms_step):
+    """Reduced-precision option, reported separately: FP8 E4M3 state + per-row fp32
+    scales (132 bytes per 128-element row). value = fp8 state bytes moved per second."""
+    from flashinfer_bench_tma_thrust_b200 import decode
+    codes, sc = decode.quantize_state_fp8(x.state)
+    holder = {"c": codes, "s": sc}
+
+    def step():
+        _, c, s = decode.kernel_fp8_state(x.q, x.k, x.v, holder["c"], holder["s"], x.A_log, x.a,
+                                          x.dt_bias, x.b, x.scale)
+        holder["c"], holder["s"] = c, s
+
+    ms = time_steps(step, K, Wm, device, world)
+    ms_step = ms / K
+    b8 = info["state_bytes"] // 4 + info["state_bytes"] // (4 * 128)
+    return {"value": round(world * b8 / (ms_step * 1e-3) / 1e9, 2),
+            "unit": "GB/s (fp8 state + row scales)", "ms_per_step": round(ms_step, 5),
+            "speedup_vs_fp32_state": round(fp32_ms_step / ms_step, 3),
+            "error": "separately reported: see tests/test_decode_fp8_state_gpu.py"}
 
 
 def prefill_measure(workload, K, Wm, device, world, rank, peak, peak_src, brief=False):

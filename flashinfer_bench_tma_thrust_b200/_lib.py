@@ -39,6 +39,12 @@ SIGNATURES = {
          _p, _int, _p, _int, _p, _int, _p, _int,
          _f32, _p, _p, _i64, _i32, _i32, _i32, _p],
     ),
+    "gdn_decode_fwd_fp8state": (
+        _int,
+        [_p, _p, _p, _p, _p,
+         _p, _int, _p, _int, _p, _int, _p, _int,
+         _f32, _p, _p, _p, _i64, _i32, _i32, _i32, _p],
+    ),
     "gdn_prefill_recurrent_fwd": (
         _int,
         [_p, _p, _p, _p,

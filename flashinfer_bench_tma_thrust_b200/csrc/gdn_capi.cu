@@ -165,6 +165,45 @@ int gdn_decode_fwd_bf16state(const void* q, const void* k, const void* v, const 
   return launch_status(gdn::launch_decode(p, static_cast<cudaStream_t>(stream)));
 }
 
+int gdn_decode_fwd_fp8state(const void* q, const void* k, const void* v, const void* state,
+                            const float* state_scale, const void* A_log, int A_log_dtype,
+                            const void* a, int a_dtype, const void* dt_bias, int dt_bias_dtype,
+                            const void* b, int b_dtype, float scale, void* out, void* new_state,
+                            float* new_state_scale, int64_t B, int32_t HQ, int32_t HV,
+                            int32_t D, void* stream) {
+  if (B < 0) return GDN_ERR_INVALID_ARG;
+  int rc = check_heads(HQ, HV, D);
+  if (rc != GDN_OK) return rc;
+  if (!gate_dtype_ok(A_log_dtype) || !gate_dtype_ok(a_dtype) || !gate_dtype_ok(dt_bias_dtype) ||
+      !gate_dtype_ok(b_dtype))
+    return GDN_ERR_UNSUPPORTED_DTYPE;
+  if (B == 0) return GDN_OK;
+  if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !out || !new_state ||
+      !new_state_scale || (state && !state_scale))
+    return GDN_ERR_INVALID_ARG;
+  gdn::DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.state_any = state;
+  p.new_state_any = new_state;
+  p.A_log = A_log;
+  p.a = a;
+  p.dt_bias = dt_bias;
+  p.b = b;
+  p.A_log_dtype = A_log_dtype;
+  p.a_dtype = a_dtype;
+  p.dt_bias_dtype = dt_bias_dtype;
+  p.b_dtype = b_dtype;
+  p.scale = resolve_scale(scale, D);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.B = B;
+  p.HQ = HQ;
+  p.HV = HV;
+  return launch_status(
+      gdn::launch_decode_fp8(p, state_scale, new_state_scale, static_cast<cudaStream_t>(stream)));
+}
+
 int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* v, const float* state,
                               const void* A_log, int A_log_dtype, const void* a, int a_dtype,
                               const void* dt_bias, int dt_bias_dtype, const void* b,

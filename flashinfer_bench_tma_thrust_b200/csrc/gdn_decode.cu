@@ -16,6 +16,8 @@
 // The state is read once and written once; nothing is staged through shared
 // memory. Rows of one head are split over several thread blocks when the batch
 // is small so that all 148 SMs get work.
+#include <cuda_fp16.h>
+
 #include "gdn_common.cuh"
 #include "gdn_launch.h"
 
@@ -155,6 +157,164 @@ int launch_decode_t(const DecodeParams& p_in, cudaStream_t stream) {
 int launch_decode(const DecodeParams& p, cudaStream_t stream) {
   return p.state_bf16 ? launch_decode_t<__nv_bfloat16>(p, stream)
                       : launch_decode_t<float>(p, stream);
+}
+
+}  // namespace gdn
+
+namespace gdn {
+
+// ---------------------------------------------------------------- fp8 state option
+// State rows stored as FP8 E4M3 with one fp32 scale per row (S[v][k] = fp8[v][k] *
+// scale[v]): 132 bytes per 128-element row instead of 512. The row is dequantised,
+// updated in fp32 exactly as in decode_kernel, the output is read from the fp32 row,
+// and the new row is requantised with scale = max|row| / 448 (E4M3's largest finite
+// value), round to nearest, saturating.
+namespace {
+
+__device__ __forceinline__ float4 fp8x4_to_f4(uint32_t w, float s) {
+  float4 r;
+  uint32_t lo2, hi2;  // two halves -> two f16x2 pairs
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo2), "=r"(hi2)
+      : "r"(w));
+  const __half2 h01 = *reinterpret_cast<const __half2*>(&lo2);
+  const __half2 h23 = *reinterpret_cast<const __half2*>(&hi2);
+  const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+  r.x = f01.x * s;
+  r.y = f01.y * s;
+  r.z = f23.x * s;
+  r.w = f23.y * s;
+  return r;
+}
+
+__device__ __forceinline__ uint32_t f4_to_fp8x4(float4 v, float inv_s) {
+  uint16_t a, b;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(a) : "f"(v.y * inv_s), "f"(v.x * inv_s));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(b) : "f"(v.w * inv_s), "f"(v.z * inv_s));
+  return static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
+}
+
+// One warp handles 4 rows per step: lane = 8 * sub + seg, sub = row in the group,
+// seg = 16-element segment; a 16-byte load brings 16 E4M3 codes. Dot products and
+// the row maximum reduce over the 8 lanes of a row (3 shuffles). G groups of 4 rows
+// are loaded before any is processed (memory-level parallelism).
+template <int G>
+__global__ void __launch_bounds__(128) decode_fp8_kernel(DecodeParams p, const float* scale_in,
+                                                          float* scale_out) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int sub = lane >> 3, seg = lane & 7;
+  const int64_t head = blockIdx.x / p.splits;
+  const int split = blockIdx.x - head * p.splits;
+  const int64_t bi = head / p.HV;
+  const int h = static_cast<int>(head - bi * p.HV);
+  const int qh = h / (p.HV / p.HQ);
+  const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
+  const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
+  const float g = expf(gate_log_decay(A_log, load_scalar(p.a, p.a_dtype, head), dtb));
+  const float beta = gate_beta(load_scalar(p.b, p.b_dtype, head));
+  const int64_t qk_off = (bi * p.HQ + qh) * kHeadDim + seg * 16;
+  float qf[16], kf[16];
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) {
+    const float4 q4 = load_bf16x4(p.q + qk_off + i), k4 = load_bf16x4(p.k + qk_off + i);
+    qf[i] = q4.x; qf[i + 1] = q4.y; qf[i + 2] = q4.z; qf[i + 3] = q4.w;
+    kf[i] = k4.x; kf[i + 1] = k4.y; kf[i + 2] = k4.z; kf[i + 3] = k4.w;
+  }
+  float kq = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) kq = fmaf(qf[i], kf[i], kq);
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
+  const int rows_per_warp = p.rows_per_warp;
+  const int row0 = (split * 4 + warp) * rows_per_warp;
+  const int64_t vrow_base = head * kHeadDim;
+  const uint4* src = static_cast<const uint4*>(p.state_any);
+  uint4* dst = static_cast<uint4*>(p.new_state_any);
+  for (int r0 = 0; r0 < rows_per_warp; r0 += 4 * G) {
+    uint4 cw[G];
+    float sc[G], vin[G];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      const int64_t row = vrow_base + row0 + r0 + 4 * gi + sub;
+      if (src) {
+        asm volatile("ld.global.cs.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(cw[gi].x), "=r"(cw[gi].y), "=r"(cw[gi].z), "=r"(cw[gi].w)
+                     : "l"(src + row * 8 + seg));
+        sc[gi] = scale_in[row];
+      } else {
+        cw[gi] = make_uint4(0u, 0u, 0u, 0u);
+        sc[gi] = 0.f;
+      }
+      const unsigned short raw = reinterpret_cast<const unsigned short*>(p.v)[row];
+      vin[gi] = __uint_as_float(static_cast<uint32_t>(raw) << 16);
+    }
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      float s[16];
+      const uint32_t w[4] = {cw[gi].x, cw[gi].y, cw[gi].z, cw[gi].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float4 f = fp8x4_to_f4(w[e], sc[gi]);
+        s[4 * e] = f.x; s[4 * e + 1] = f.y; s[4 * e + 2] = f.z; s[4 * e + 3] = f.w;
+      }
+      float sk = 0.f, sq = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        sk = fmaf(s[i], kf[i], sk);
+        sq = fmaf(s[i], qf[i], sq);
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      }
+      const float delta = beta * (vin[gi] - g * sk);
+      float m = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        s[i] = fmaf(g, s[i], delta * kf[i]);
+        m = fmaxf(m, fabsf(s[i]));
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float nsc = m > 0.f ? m * (1.0f / 448.0f) : 1.0f;
+      const float inv = 1.0f / nsc;
+      uint4 ow;
+      ow.x = f4_to_fp8x4(make_float4(s[0], s[1], s[2], s[3]), inv);
+      ow.y = f4_to_fp8x4(make_float4(s[4], s[5], s[6], s[7]), inv);
+      ow.z = f4_to_fp8x4(make_float4(s[8], s[9], s[10], s[11]), inv);
+      ow.w = f4_to_fp8x4(make_float4(s[12], s[13], s[14], s[15]), inv);
+      const int64_t row = vrow_base + row0 + r0 + 4 * gi + sub;
+      asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(dst + row * 8 + seg),
+                   "r"(ow.x), "r"(ow.y), "r"(ow.z), "r"(ow.w)
+                   : "memory");
+      if (seg == 0) {
+        scale_out[row] = nsc;
+        p.out[row] = __float2bfloat16_rn(p.scale * fmaf(g, sq, delta * kq));
+      }
+    }
+  }
+}
+
+}  // namespace
+
+int launch_decode_fp8(const DecodeParams& p_in, const float* scale_in, float* scale_out,
+                      cudaStream_t stream) {
+  DecodeParams p = p_in;
+  const int64_t heads = p.B * p.HV;
+  if (heads == 0) return 0;
+  int splits = 1;
+  while (splits < 8 && heads * splits < 148 * 4) splits *= 2;
+  p.splits = splits;
+  p.rows_per_warp = kHeadDim / (4 * splits);
+  const dim3 grid(static_cast<unsigned>(heads * splits));
+  if (p.rows_per_warp >= 16)
+    decode_fp8_kernel<4><<<grid, 128, 0, stream>>>(p, scale_in, scale_out);
+  else
+    decode_fp8_kernel<1><<<grid, 128, 0, stream>>>(p, scale_in, scale_out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace gdn

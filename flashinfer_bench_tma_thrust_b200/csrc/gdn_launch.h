@@ -51,6 +51,8 @@ struct PrefillParams {
 };
 
 int launch_decode(const DecodeParams& p, cudaStream_t stream);
+int launch_decode_fp8(const DecodeParams& p, const float* scale_in, float* scale_out,
+                      cudaStream_t stream);
 int launch_prefill_recurrent(const PrefillParams& p, cudaStream_t stream);
 int launch_prefill_chunked(const PrefillParams& p, cudaStream_t stream);
 size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV);

@@ -143,3 +143,57 @@ def kernel_multitoken(q, k, v, state, A_log, a, dt_bias, b, scale=None):
                                     a.reshape(B * T, HV), dt_bias, b.reshape(B * T, HV), cu,
                                     scale)
     return out.view(B, T, HV, D), new_state
+
+
+def quantize_state_fp8(state: torch.Tensor):
+    """fp32 state [..., V, K] -> (E4M3 codes as uint8, fp32 per-row scales [..., V]),
+    the layout of ``kernel_fp8_state`` (scale = max|row| / 448)."""
+    s = state.float()
+    amax = s.abs().amax(dim=-1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    codes = (s / scale[..., None]).to(torch.float8_e4m3fn).view(torch.uint8)
+    return codes, scale
+
+
+def dequantize_state_fp8(codes: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    return codes.view(torch.float8_e4m3fn).float() * scale[..., None]
+
+
+def kernel_fp8_state(q, k, v, state_codes, state_scale, A_log, a, dt_bias, b, scale=None):
+    """Reduced-precision option: decode with an FP8 E4M3 state (uint8 codes
+    [B, HV, 128, 128] + fp32 per-row scales [B, HV, 128]). fp32 math; the new state is
+    requantised per row. ~3.9x fewer state bytes than fp32, with its own error (see
+    tests/test_decode_fp8_state_gpu.py). Returns (output, new_codes, new_scales)."""
+    dev = q.device
+    B, T, HQ, D = q.shape
+    if T != 1:
+        raise ValueError(f"decode expects seq_len 1 (q.shape[1]), got {T}")
+    HV = v.shape[2]
+    C.check_heads(HQ, HV, D)
+    for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a),
+                    ("dt_bias", dt_bias), ("b", b)):
+        C.require_cuda(name, t, dev)
+    if state_codes is not None:
+        if state_codes.dtype != torch.uint8 or tuple(state_codes.shape) != (B, HV, D, D):
+            raise ValueError("state codes must be uint8 [B, HV, 128, 128]")
+        if state_scale is None or tuple(state_scale.shape) != (B, HV, D):
+            raise ValueError("state scales must be fp32 [B, HV, 128]")
+        state_codes = state_codes.contiguous()
+        state_scale = state_scale.float().contiguous()
+    q_c, k_c, v_c = C.as_bf16("q", q), C.as_bf16("k", k), C.as_bf16("v", v)
+    A_c, A_t = C.as_gate("A_log", A_log)
+    a_c, a_t = C.as_gate("a", a)
+    d_c, d_t = C.as_gate("dt_bias", dt_bias)
+    b_c, b_t = C.as_gate("b", b)
+    out = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=dev)
+    new_codes = torch.empty(B, HV, D, D, dtype=torch.uint8, device=dev)
+    new_scale = torch.empty(B, HV, D, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.gdn_decode_fwd_fp8state(
+            q_c.data_ptr(), k_c.data_ptr(), v_c.data_ptr(), C.ptr(state_codes),
+            C.ptr(state_scale), A_c.data_ptr(), A_t, a_c.data_ptr(), a_t, d_c.data_ptr(), d_t,
+            b_c.data_ptr(), b_t, C.resolve_scale(scale, D), out.data_ptr(), new_codes.data_ptr(),
+            new_scale.data_ptr(), B, HQ, HV, D, C.stream_handle(dev))
+    _lib.check(rc, "gdn_decode_fwd_fp8state")
+    return out, new_codes, new_scale

@@ -97,6 +97,23 @@ GDN_API int gdn_decode_fwd_bf16state(const void* q, const void* k, const void* v
                                      int32_t HV, int32_t D, void* stream);
 
 /*
+ * Decode with an FP8 (E4M3) recurrent state and one fp32 scale per state row
+ * (reduced-precision option, reported separately): state / new_state uint8
+ * [B, HV, D, D] k-last holding E4M3 codes, state_scale / new_state_scale fp32
+ * [B, HV, D] with S[v][k] = code[v][k] * scale[v]. fp32 math; the new row is
+ * requantised with scale = max|row| / 448. Counterpart of the reference's
+ * gdn_decode_kernel_v10_fp8 (gdn/kernels/cute_cpp/gdn_decode_v10.cuh:666-862).
+ * state may be NULL (zeros); new_state / new_state_scale may alias the inputs.
+ */
+GDN_API int gdn_decode_fwd_fp8state(const void* q, const void* k, const void* v,
+                                    const void* state, const float* state_scale,
+                                    const void* A_log, int A_log_dtype, const void* a,
+                                    int a_dtype, const void* dt_bias, int dt_bias_dtype,
+                                    const void* b, int b_dtype, float scale, void* out,
+                                    void* new_state, float* new_state_scale, int64_t B,
+                                    int32_t HQ, int32_t HV, int32_t D, void* stream);
+
+/*
  * Variable-length prefill over cu_seqlens-packed sequences, token-sequential
  * recurrence (one thread block per sequence, v-head and 32-row V tile, the
  * state tile held in registers across the whole sequence).

@@ -1,0 +1,60 @@
+"""Reduced-precision decode option: FP8 E4M3 state with per-row fp32 scales,
+reported separately from the fp32 path with its own error (the measurement of
+the reference's quantisation study, gdn/tests/test_quantization_accuracy.py:219-330).
+Single step: the kernel's dequantisation, update and output equal the oracle run
+on the dequantised input state; its stored new state is the E4M3 rounding of the
+oracle's fp32 new state (per-row scale max|row|/448). Long run: error of 100
+steps against the fp32 path, bounded."""
+import pytest
+import torch
+
+from flashinfer_bench_tma_thrust_b200 import decode, workloads as W
+from oracle import gdn_oracle
+from parity import assert_out_close, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("B", [1, 16, 64])
+def test_fp8_state_single_step(B):
+    x = W.decode_inputs(B, seed=300 + B)
+    codes, sc = decode.quantize_state_fp8(x.state)
+    deq = decode.dequantize_state_fp8(codes, sc)
+    ref_out, ref_state = gdn_oracle.decode(x.q, x.k, x.v, deq, x.A_log, x.a, x.dt_bias, x.b,
+                                           x.scale)
+    xd = to_dev(x)
+    out, ncodes, nsc = decode.kernel_fp8_state(xd.q, xd.k, xd.v, codes.cuda(), sc.cuda(),
+                                               xd.A_log, xd.a, xd.dt_bias, xd.b, xd.scale)
+    assert_out_close(out, ref_out, "fp8-state output")
+    got = decode.dequantize_state_fp8(ncodes.cpu(), nsc.cpu())
+    # scales: max|row| / 448 of the fp32 new state
+    ref_sc = ref_state.abs().amax(-1) / 448.0
+    assert torch.allclose(nsc.cpu(), ref_sc, rtol=1e-4, atol=1e-12)
+    # each element within half an E4M3 step (3 mantissa bits) of the fp32 value
+    step = torch.clamp(ref_state.abs(), min=ref_sc[..., None] * 2.0 ** -6) * 2.0 ** -3
+    assert ((got - ref_state).abs() <= step * 0.5 + 1e-7).float().mean() > 0.999
+
+
+def test_fp8_state_error_over_100_steps():
+    B, steps = 8, 100
+    x = to_dev(W.decode_inputs(B, seed=9))
+    s32 = x.state.clone()
+    codes, sc = decode.quantize_state_fp8(x.state)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    max_out_rel = 0.0
+    for _ in range(steps):
+        q = torch.nn.functional.normalize(torch.randn(B, 1, 16, 128, device="cuda", generator=g), dim=-1).to(torch.bfloat16)
+        k = torch.nn.functional.normalize(torch.randn(B, 1, 16, 128, device="cuda", generator=g), dim=-1).to(torch.bfloat16)
+        v = torch.randn(B, 1, 32, 128, device="cuda", generator=g).to(torch.bfloat16)
+        a = torch.randn(B, 1, 32, device="cuda", generator=g).to(torch.bfloat16)
+        b = torch.randn(B, 1, 32, device="cuda", generator=g).to(torch.bfloat16)
+        o32, s32 = decode.kernel(q, k, v, s32, x.A_log, a, x.dt_bias, b, x.scale)
+        o8, codes, sc = decode.kernel_fp8_state(q, k, v, codes, sc, x.A_log, a, x.dt_bias, b,
+                                                x.scale)
+        rel = ((o8.float() - o32.float()).norm() / o32.float().norm()).item()
+        max_out_rel = max(max_out_rel, rel)
+    s8 = decode.dequantize_state_fp8(codes, sc)
+    state_rel = ((s8 - s32).norm() / s32.norm()).item()
+    print(f"fp8 state, {steps} steps: max output rel err {max_out_rel:.2e}, "
+          f"final state rel err {state_rel:.2e}")
+    assert state_rel < 0.1 and max_out_rel < 0.1
