@@ -66,6 +66,7 @@ SIGNATURES = {
          _p, _int, _f32, _p, _p, _i64, _i64, _i32, _i32, _i32, _p],
     ),
     "gdn_selftest_umma": (_int, [_p, _p, _p, _int, _int, _p, _p]),
+    "gdn_selftest_wait_timeout": (_int, [_p, _p, _p]),
 }
 
 _lock = threading.Lock()

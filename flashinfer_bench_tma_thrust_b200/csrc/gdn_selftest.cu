@@ -102,3 +102,33 @@ extern "C" int gdn_selftest_umma(const void* A, const void* B, float* D, int a_m
       b_mn_major, status);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
+
+namespace gdn {
+namespace {
+
+// Waits on an mbarrier phase that nothing completes: the bounded wait must give up
+// (after about a second) and the kernel must report it instead of hanging.
+__global__ void wait_timeout_kernel(int* status, long long* waited_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  const uint64_t t0 = sm100::globaltimer_ns();
+  const bool ok = sm100::mbar_wait(&bar, 0);
+  const uint64_t t1 = sm100::globaltimer_ns();
+  if (threadIdx.x == 0) {
+    *status = ok ? 0 : 1;
+    *waited_ns = static_cast<long long>(t1 - t0);
+  }
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_selftest_wait_timeout(int* status, long long* waited_ns, void* stream) {
+  if (!status || !waited_ns) return GDN_ERR_INVALID_ARG;
+  gdn::wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, waited_ns);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}

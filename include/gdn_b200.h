@@ -222,6 +222,14 @@ GDN_API int gdn_prefill_chunked_fwd_noalloc(const void* q, const void* k, const 
 GDN_API int gdn_selftest_umma(const void* A, const void* B, float* D, int a_mn_major,
                               int b_mn_major, int* status, void* stream);
 
+/*
+ * Diagnostics. The bounded mbarrier wait used by every kernel here, run on a
+ * barrier that nothing arrives on (no counterpart in the reference): the wait
+ * gives up after about one second, *status (device int) becomes 1 and
+ * *waited_ns (device int64) holds the time waited; the context stays usable.
+ */
+GDN_API int gdn_selftest_wait_timeout(int* status, long long* waited_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

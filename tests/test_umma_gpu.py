@@ -25,3 +25,19 @@ def test_umma_gemm_128x64x128(a_mn, b_mn):
     assert status.item() == 0, "MMA completion wait timed out"
     ref = A.float() @ B.float()
     assert torch.allclose(D, ref, atol=1e-3, rtol=1e-4), (D - ref).abs().max().item()
+
+
+def test_bounded_wait_gives_up_and_context_survives():
+    """A wait on an mbarrier phase that never completes returns after ~1 s with an
+    error status (no hang, no trap); the GPU context keeps working afterwards."""
+    lib = _lib.load()
+    status = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    waited = torch.zeros(1, dtype=torch.int64, device="cuda")
+    rc = lib.gdn_selftest_wait_timeout(status.data_ptr(), waited.data_ptr(),
+                                       torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "gdn_selftest_wait_timeout")
+    torch.cuda.synchronize()
+    assert status.item() == 1
+    assert 0.9e9 <= waited.item() <= 5e9, waited.item()
+    x = torch.ones(1024, device="cuda")  # the context is still usable
+    assert (x * 2).sum().item() == 2048
