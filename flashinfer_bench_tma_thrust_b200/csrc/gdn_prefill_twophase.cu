@@ -117,6 +117,29 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
   }
 }
 
+// ------------------------------------------------------------------ scan order
+// order[i] = the sequence the i-th group of scan blocks processes: longest first
+// (most chunks), ties by index, so that the longest chains start in the first wave
+// and short ones fill the tail. Rank sort, one thread per sequence (N <= kMaxSortN;
+// beyond that the identity order).
+constexpr int64_t kMaxSortN = 4096;
+__global__ void __launch_bounds__(256) scan_order_kernel(int64_t N, const int64_t* offs,
+                                                         int32_t* order) {
+  const int64_t n = blockIdx.x * 256 + threadIdx.x;
+  if (n >= N) return;
+  if (N > kMaxSortN) {
+    order[n] = static_cast<int32_t>(n);
+    return;
+  }
+  const int64_t cn = offs[n + 1] - offs[n];
+  int64_t rank = 0;
+  for (int64_t m = 0; m < N; ++m) {
+    const int64_t cm = offs[m + 1] - offs[m];
+    rank += (cm > cn || (cm == cn && m < n)) ? 1 : 0;
+  }
+  order[rank] = static_cast<int32_t>(n);
+}
+
 // ------------------------------------------------------------------ prep
 // 256 threads; thread t owns TMEM lane / row t % 128 and a 32-column half of it.
 // Shared memory: the K/Q tile (32 KB, TMA) is dead after S and then holds the fp32 A
@@ -318,7 +341,8 @@ __device__ __forceinline__ void tmem_ld32w(uint32_t taddr, float (&r)[32]) {
 
 __global__ void __launch_bounds__(kScanThreads, 2)
     scan_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
-                const int64_t* __restrict__ offs, const uint8_t* __restrict__ a2_in) {
+                const int64_t* __restrict__ offs, const int32_t* __restrict__ order,
+                const uint8_t* __restrict__ a2_in) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
@@ -336,7 +360,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
   const int64_t unit = blockIdx.x;
   const int vt = static_cast<int>(unit % kTiles);
   const int h = static_cast<int>((unit / kTiles) % p.HV);
-  const int64_t n = unit / (kTiles * p.HV);
+  const int64_t n = order[unit / (kTiles * p.HV)];
   const int qh = h / (p.HV / p.HQ);
   const int64_t HV = p.HV;
   int64_t start, end;
@@ -575,8 +599,15 @@ __global__ void __launch_bounds__(kScanThreads, 2)
 
 }  // namespace
 
+// Workspace: [0, 256) status word; [256, ...) chunk offsets (N + 1 int64), then the
+// scan order (N int32); then, 1024-aligned, 24 KB of [T_b; P] per (chunk, v-head).
+static size_t head_bytes(int64_t N) {
+  return (256 + 8 * static_cast<size_t>(N + 1) + 4 * static_cast<size_t>(N) + 1023) &
+         ~size_t(1023);
+}
+
 size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV) {
-  const size_t head = (256 + 8 * static_cast<size_t>(N + 1) + 1023) & ~size_t(1023);
+  const size_t head = head_bytes(N);
   const size_t chunks = static_cast<size_t>((T + kC - 1) / kC + N);
   return head + chunks * static_cast<size_t>(HV) * kA2Bytes;
 }
@@ -585,7 +616,8 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   if (p.N == 0) return 0;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int64_t* offs = reinterpret_cast<int64_t*>(ws + 256);
-  const size_t head = (256 + 8 * static_cast<size_t>(p.N + 1) + 1023) & ~size_t(1023);
+  int32_t* order = reinterpret_cast<int32_t*>(ws + 256 + 8 * (p.N + 1));
+  const size_t head = head_bytes(p.N);
   uint8_t* a2 = ws + head;
   ChunkTmaps maps;
   const int64_t Tm = p.T > 0 ? p.T : 1;
@@ -598,12 +630,15 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
           cudaSuccess)
     return -1;
   chunk_offsets_kernel<<<1, 1024, 0, stream>>>(p, offs);
+  scan_order_kernel<<<static_cast<unsigned>((p.N + 255) / 256), 256, 0, stream>>>(p.N, offs,
+                                                                                 order);
   const int64_t cap = (p.T + kC - 1) / kC + p.N;
   if (p.T > 0) {
     prep_kernel<<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(p, maps, offs, a2);
   }
   scan_kernel<<<static_cast<unsigned>(p.N * p.HV * kTiles), kScanThreads, kScanSmem, stream>>>(p, maps,
-                                                                                     offs, a2);
+                                                                                     offs, order,
+                                                                                     a2);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
