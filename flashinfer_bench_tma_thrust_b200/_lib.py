@@ -67,6 +67,7 @@ SIGNATURES = {
     ),
     "gdn_selftest_umma": (_int, [_p, _p, _p, _int, _int, _p, _p]),
     "gdn_selftest_wait_timeout": (_int, [_p, _p, _p]),
+    "gdn_selftest_umma_ts": (_int, [_p, _p, _p, _p, _p]),
 }
 
 _lock = threading.Lock()

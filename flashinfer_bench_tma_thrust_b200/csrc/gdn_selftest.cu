@@ -87,8 +87,87 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
   if (warp == 0) tmem_dealloc(tbase, 64);
 }
 
+// A from TMEM (written by tcgen05.st, row m in lane m, bf16 pairs per column), B
+// K-major from shared memory: D[128 x N] = A[128 x 128] B[128 x N], N = 128.
+__global__ void __launch_bounds__(128) umma_ts_selftest_kernel(const __nv_bfloat16* A,
+                                                               const __nv_bfloat16* B, float* D,
+                                                               int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sB = smem;  // 2 k-halves x 128 rows (n) x 128 B = 32 KB
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  const int t = threadIdx.x;
+  const int warp = t >> 5;
+  for (int idx = t; idx < 128 * 128; idx += 128) {
+    const int k = idx / 128, n = idx % 128;  // B given as [k][n] row-major
+    *reinterpret_cast<__nv_bfloat16*>(sB + (k / 64) * 16384 + sw128_offset(n, k % 64)) = B[idx];
+  }
+  if (t == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, 256);
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base;
+  const uint32_t lane_addr = tbase + ((warp * 32u) << 16);
+  // A row t -> columns [128, 192) of lane t: 64 words of two bf16
+  for (int c0 = 0; c0 < 64; c0 += 32) {
+    float w[32];
+    for (int j = 0; j < 32; ++j) {
+      const int c = c0 + j;
+      const uint32_t lo = __bfloat16_as_ushort(A[t * 128 + 2 * c]);
+      const uint32_t hi = __bfloat16_as_ushort(A[t * 128 + 2 * c + 1]);
+      w[j] = __uint_as_float(lo | (hi << 16));
+    }
+    tmem_st32(lane_addr + 128 + c0, w);
+  }
+  tmem_st_wait();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (t == 0) {
+    const uint32_t idesc = idesc_bf16(128, 128, false, false);
+    for (int s = 0; s < 8; ++s)
+      mma_bf16_ts(tbase, tbase + 128 + s * 8,
+                  desc_kmajor(smem_u32(sB) + (s / 4) * 16384 + (s % 4) * 32), idesc, s > 0);
+    mma_commit(&bar);
+  }
+  const bool ok = mbar_wait(&bar, 0);
+  tc_fence_after();
+  if (!ok) {
+    if (t == 0) atomicExch(status, 1);
+  } else {
+    for (int c = 0; c < 128; c += 32) {
+      float r[32];
+      tmem_ld32(lane_addr + c, r);
+      tmem_ld_wait();
+      for (int j = 0; j < 32; ++j) D[t * 128 + c + j] = r[j];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 256);
+}
+
 }  // namespace
 }  // namespace gdn
+
+extern "C" int gdn_selftest_umma_ts(const void* A, const void* B, float* D, int* status,
+                                    void* stream) {
+  if (!A || !B || !D || !status) return GDN_ERR_INVALID_ARG;
+  const int smem = 32768 + 1024;
+  if (cudaFuncSetAttribute(gdn::umma_ts_selftest_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return GDN_ERR_CUDA;
+  gdn::umma_ts_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(B), D, status);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
 
 extern "C" int gdn_selftest_umma(const void* A, const void* B, float* D, int a_mn_major,
                                  int b_mn_major, int* status, void* stream) {

@@ -223,6 +223,15 @@ GDN_API int gdn_selftest_umma(const void* A, const void* B, float* D, int a_mn_m
                               int b_mn_major, int* status, void* stream);
 
 /*
+ * Diagnostics. Known-answer check of the tensor-core product with A read from
+ * tensor memory (no counterpart in the reference): D[128x128] fp32 =
+ * A[128x128] x B[128x128], bf16 row-major inputs ([m][k] and [k][n]); A is
+ * stored into TMEM row by row (two bf16 per 32-bit column), B in shared memory.
+ */
+GDN_API int gdn_selftest_umma_ts(const void* A, const void* B, float* D, int* status,
+                                 void* stream);
+
+/*
  * Diagnostics. The bounded mbarrier wait used by every kernel here, run on a
  * barrier that nothing arrives on (no counterpart in the reference): the wait
  * gives up after about one second, *status (device int) becomes 1 and

@@ -41,3 +41,20 @@ def test_bounded_wait_gives_up_and_context_survives():
     assert 0.9e9 <= waited.item() <= 5e9, waited.item()
     x = torch.ones(1024, device="cuda")  # the context is still usable
     assert (x * 2).sum().item() == 2048
+
+
+def test_umma_a_from_tmem_128x128x128():
+    """tcgen05.mma with A read from tensor memory (the form of the transposed products)."""
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(5)
+    A = torch.randn(128, 128, generator=g).to(torch.bfloat16).cuda()
+    B = torch.randn(128, 128, generator=g).to(torch.bfloat16).cuda()
+    D = torch.full((128, 128), float("nan"), device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = lib.gdn_selftest_umma_ts(A.data_ptr(), B.data_ptr(), D.data_ptr(), status.data_ptr(),
+                                  torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "gdn_selftest_umma_ts")
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref = A.float() @ B.float()
+    assert torch.allclose(D, ref, atol=1e-3, rtol=1e-4), (D - ref).abs().max().item()
