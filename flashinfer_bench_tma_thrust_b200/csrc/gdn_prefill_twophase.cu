@@ -10,15 +10,17 @@
 //     S = [K;Q] K^T, A, M, T_b = (I + A)^-1 diag(beta), [T_b; P] = [I; M] T_b
 //     -> the bf16 image of [T_b; P] (hi 128 rows, lo rows 0..63: 24 KB) written to
 //        the workspace in the 128B-swizzled layout the scan kernel's MMA reads.
-//   scan (one block per (sequence, v-head, 64-wide V tile), chunk by chunk):
+//   scan (one 256-thread block per (sequence, v-head), chunk by chunk; the products
+//   are taken transposed so that the chain's own operands live in TMEM):
 //     [KH; QH] = [K;Q] H,  X = V - gamma KH,  [U; O'] = [T_b; P] X,
 //     O = scale (gamma QH + O'),  H <- gamma_last H + K^T diag(f) U.
 //
 // The prep phase has (T/64 + N) x HV independent blocks, so the triangular solve
 // and the operand construction run at full occupancy instead of on the critical
 // path of each sequence; the scan keeps only the state chain and receives
-// [T_b; P] with one bulk copy per chunk. P enters the tensor core as hi only (its
-// rounding only touches the output, which is bf16), T_b as hi + lo.
+// [T_b; P] with one bulk copy per chunk, double-buffered with the K/Q and V tiles.
+// P enters the tensor core as hi only (its rounding only touches the output, which
+// is bf16), T_b as hi + lo.
 // A tiny first kernel turns cu_seqlens into per-sequence chunk offsets so that
 // no host synchronisation is needed.
 #include "gdn_chunk_common.cuh"
@@ -289,155 +291,174 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
   if (warp == 0) tmem_dealloc(tmem, kPrepTmemCols);
 }
 
-// ------------------------------------------------------------------ scan
-// Shared memory: KQ tile (32 KB; its Q halves hold X and then diag(f) U),
-// H hi/lo (32 KB), [T_b; P] hi/lo (32 KB; lo rows 64..127 stay zero).
-// 256 threads: thread t owns TMEM lane / operand row r = t % 128 and the 32
-// columns [32 c, 32 c + 32) of it, c = t / 128 (warps w and w + 4 share lanes).
-constexpr uint32_t S_OFF_KQ = 0;
-constexpr uint32_t S_OFF_X_HI = 8192;
-constexpr uint32_t S_OFF_X_LO = 24576;
-constexpr uint32_t S_OFF_H_HI = 32768;
-constexpr uint32_t S_OFF_H_LO = 49152;
-constexpr uint32_t S_OFF_A2_HI = 65536;
-constexpr uint32_t S_OFF_A2_LO = 81920;
-constexpr uint32_t S_OFF_G = 98304;  // 2 x 64 fp32 (double-buffered by chunk parity)
-constexpr uint32_t S_OFF_BETA = 98816;  // 2 x 64 fp32 (written by the gate scan, unused here)
-constexpr uint32_t S_OFF_BAR = 99328;
-constexpr uint32_t kScanSmem = 99392 + 1024;
-constexpr uint32_t kScanTmemCols = 256;
-constexpr uint32_t ST_1 = 64, ST_2 = 128, ST_3 = 192;  // columns 0..63 unused
-constexpr int kScanThreads = 256;
-// Thread that issues the MMAs, TMA and bulk copies: warp 3 (rows 96..127), whose own
-// per-chunk work (output rows) is off the state chain, so the cycles it spends
-// blocked on MMA issue do not delay the chain's conversions.
-constexpr int kIssuer = 96;
-// Warps 4-5 (threads 128..191, idle while the state-update MMA runs) load the raw
-// gates and compute the next chunk's decays.
-constexpr int kGateBase = 128;
-constexpr int kHalf = kVT / 2;  // columns per thread
+// ------------------------------------------------------------------ scan, transposed
+// One 256-thread block per (sequence, v-head): the whole 128 x 128 state. The
+// products are taken transposed so that everything the chain produces is an A
+// operand read from TMEM (lane = state row v) and every B operand is a tile that
+// arrived by TMA / bulk copy:
+//   D1 = S [K;Q]^T        -> [ (KH)^T | (QH)^T ]          (A = S hi/lo from TMEM)
+//   X^T = V^T - (KH)^T diag(gamma)                         (written to TMEM as bf16 hi/lo)
+//   D2 = X^T [T_b; P]^T   -> [ U^T | (P X)^T ]
+//   U'^T = U^T diag(f);  O^T = scale ((QH)^T diag(gamma) + (P X)^T)
+//   dS = U'^T K;  S <- gamma_last S + dS                   (S = H^T, k-last, in registers)
+// Thread t owns state row v = t % 128 and half c = t / 128 of every row-sliced
+// quantity (k in [64c, 64c+64) of S; j in [32c, 32c+32) of X, U; i likewise of O).
+// K/Q, V and [T_b; P] are double-buffered: chunk c+1's tiles are requested when
+// chunk c starts.
+constexpr uint32_t T_OFF_KQ = 0;          // 2 x 32 KB
+constexpr uint32_t T_OFF_A2 = 65536;      // 2 x 32 KB: hi 16 KB | lo 16 KB (rows 64..127 zero)
+constexpr uint32_t T_OFF_V = 131072;      // 2 x 16 KB: V tile, rows j x 128 v (256 B rows)
+constexpr uint32_t T_OFF_G = 163840;      // 2 x 64 fp32
+constexpr uint32_t T_OFF_BETA = 164352;   // 2 x 64 fp32 (written by the gate scan, unused)
+constexpr uint32_t T_OFF_GAM = 164864;    // 2 x 64 fp32: gamma_j = e^{Gamma_j}
+constexpr uint32_t T_OFF_F = 165376;      // 2 x 64 fp32: f_j = e^{Gamma_last - Gamma_j} (0 if padded)
+constexpr uint32_t T_OFF_BAR = 165888;    // ld[2], a2[2], mma; TMEM slot
+constexpr uint32_t T_OFF_O = 166912;      // 2 x 16 KB: output tile, rows i x 128 v (TMA store)
+constexpr uint32_t kScanTSmem = 166912 + 32768 + 1024;
+constexpr uint32_t kScanTTmemCols = 512;
+constexpr uint32_t TT_S = 0;    // S operand: hi [0, 64) | lo [64, 128); later dS (fp32, 128)
+constexpr uint32_t TT_D1 = 128; // 128 fp32 columns
+constexpr uint32_t TT_X = 256;  // X^T then U'^T operand: hi [256, 288) | lo [288, 320)
+constexpr uint32_t TT_D2 = 320; // 128 fp32 columns
+constexpr uint32_t ID_T_K = idesc_bf16(128, 128, false, false);   // B K-major
+constexpr uint32_t ID_T_MN = idesc_bf16(128, 128, false, true);   // B MN-major
+constexpr int kScanTThreads = 256;
+constexpr int kScanTGateBase = 128;  // warps 4-5 compute the next chunk's gates
 
-// Split 32 fp32 values into bf16 hi/lo and write them as chunks [c0, c0+4) of
-// row `row` of two 128B-swizzled tiles.
-__device__ __forceinline__ void store_half_row_split(uint8_t* hi, uint8_t* lo, uint32_t row,
-                                                     uint32_t c0, const float* v) {
+struct ScanMaps {
+  CUtensorMap k, q, v, o;
+};
+
+// 2n fp32 -> n bf16x2 words, hi and lo parts
+template <int NW>
+__device__ __forceinline__ void split_words(const float* x, uint32_t (&hi)[NW], uint32_t (&lo)[NW]) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t hw[4], lw[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      split2(v[c * 8 + 2 * e], v[c * 8 + 2 * e + 1], hw[e], lw[e]);
-    }
-    const uint32_t off = sw128_chunk(row, c0 + c);
-    *reinterpret_cast<uint4*>(hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4*>(lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-  }
+  for (int w = 0; w < NW; ++w) split2(x[2 * w], x[2 * w + 1], hi[w], lo[w]);
 }
 
-__device__ __forceinline__ void tmem_ld32w(uint32_t taddr, float (&r)[32]) {
-  tmem_ld32(taddr, r);
-  tmem_ld_wait();
-}
-
-__global__ void __launch_bounds__(kScanThreads, 2)
-    scan_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
-                const int64_t* __restrict__ offs, const int32_t* __restrict__ order,
-                const uint8_t* __restrict__ a2_in) {
+__global__ void __launch_bounds__(kScanTThreads, 1)
+    scan_t_kernel(const PrefillParams p, const __grid_constant__ ScanMaps maps,
+                  const int64_t* __restrict__ offs, const int32_t* __restrict__ order,
+                  const uint8_t* __restrict__ a2_in) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  float* sG0 = reinterpret_cast<float*>(sm + S_OFF_G);
-  float* sBeta0 = reinterpret_cast<float*>(sm + S_OFF_BETA);
-  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(sm + S_OFF_BAR);
-  uint64_t* bar_a2 = bar_tma + 1;
-  uint64_t* bar_mma = bar_tma + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S_OFF_BAR + 32);
+  float* sG0 = reinterpret_cast<float*>(sm + T_OFF_G);
+  float* sBeta0 = reinterpret_cast<float*>(sm + T_OFF_BETA);
+  float* sGam0 = reinterpret_cast<float*>(sm + T_OFF_GAM);
+  float* sF0 = reinterpret_cast<float*>(sm + T_OFF_F);
+  uint64_t* bar_ld = reinterpret_cast<uint64_t*>(sm + T_OFF_BAR);  // [2]
+  uint64_t* bar_a2 = bar_ld + 2;                                   // [2]
+  uint64_t* bar_mma = bar_ld + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + T_OFF_BAR + 48);
 
   const int t = threadIdx.x, warp = t >> 5;
-  const int r = t & 127;         // row / TMEM lane
-  const int ch = t >> 7;         // column half
-  const int col0 = ch * kHalf;   // first column owned
-  const int64_t unit = blockIdx.x;
-  const int vt = static_cast<int>(unit % kTiles);
-  const int h = static_cast<int>((unit / kTiles) % p.HV);
-  const int64_t n = order[unit / (kTiles * p.HV)];
+  const int v = t & 127, ch = t >> 7;
+  const int h = static_cast<int>(blockIdx.x % p.HV);
+  const int64_t n = order[blockIdx.x / p.HV];
   const int qh = h / (p.HV / p.HQ);
   const int64_t HV = p.HV;
   int64_t start, end;
   seq_bounds(p, n, start, end);
 
-  // state rows of this tile: S[n, h, vt*64 + v, k]; this thread owns k = r, v in its half
-  const int64_t sbase = ((n * p.HV + h) * kHeadDim + vt * kVT + col0) * kHeadDim + r;
-  float hrow[kHalf];
+  // this thread's half of state row v: S[n, h, v, 64c .. 64c+64)
+  const int64_t sbase = ((n * HV + h) * kHeadDim + v) * kHeadDim + 64 * ch;
+  float S[64];
 #pragma unroll
-  for (int v = 0; v < kHalf; ++v) hrow[v] = p.state ? p.state[sbase + v * kHeadDim] : 0.0f;
+  for (int i = 0; i < 64; i += 4) {
+    const float4 x = p.state ? *reinterpret_cast<const float4*>(p.state + sbase + i)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    S[i] = x.x; S[i + 1] = x.y; S[i + 2] = x.z; S[i + 3] = x.w;
+  }
   if (end <= start) {  // empty sequence: pass the state through
 #pragma unroll
-    for (int v = 0; v < kHalf; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
+    for (int i = 0; i < 64; i += 4)
+      *reinterpret_cast<float4*>(p.new_state + sbase + i) =
+          make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
     return;
   }
   const uint8_t* a2_seq = a2_in + static_cast<uint64_t>(offs[n]) * HV * kA2Bytes +
                           static_cast<uint64_t>(h) * kA2Bytes;
   const uint64_t a2_chunk_stride = static_cast<uint64_t>(HV) * kA2Bytes;
 
-  auto issue_tma = [&](int64_t cs) {
+  auto issue_loads = [&](int64_t cs, int64_t c, int b) {
     fence_async_smem();
-    mbar_arrive_expect_tx(bar_tma, 4 * 8192);
+    uint8_t* kq = sm + T_OFF_KQ + b * 32768;
+    mbar_arrive_expect_tx(&bar_ld[b], 4 * 8192 + 16384);
     const int tok = static_cast<int>(cs);
-    tma_load_3d(sm + S_OFF_KQ, &maps.k, bar_tma, 0, qh, tok);
-    tma_load_3d(sm + S_OFF_KQ + 8192, &maps.q, bar_tma, 0, qh, tok);
-    tma_load_3d(sm + S_OFF_KQ + 16384, &maps.k, bar_tma, 64, qh, tok);
-    tma_load_3d(sm + S_OFF_KQ + 16384 + 8192, &maps.q, bar_tma, 64, qh, tok);
-  };
-  auto issue_a2 = [&](int64_t c) {
-    fence_async_smem();
-    mbar_arrive_expect_tx(bar_a2, kA2Bytes);
+    tma_load_3d(kq, &maps.k, &bar_ld[b], 0, qh, tok);
+    tma_load_3d(kq + 8192, &maps.q, &bar_ld[b], 0, qh, tok);
+    tma_load_3d(kq + 16384, &maps.k, &bar_ld[b], 64, qh, tok);
+    tma_load_3d(kq + 16384 + 8192, &maps.q, &bar_ld[b], 64, qh, tok);
+    tma_load_3d(sm + T_OFF_V + b * 16384, &maps.v, &bar_ld[b], 0, h, tok);
+    mbar_arrive_expect_tx(&bar_a2[b], kA2Bytes);
     const uint8_t* src = a2_seq + static_cast<uint64_t>(c) * a2_chunk_stride;
-    bulk_load(sm + S_OFF_A2_HI, src, 16384, bar_a2);
-    bulk_load(sm + S_OFF_A2_LO, src + 16384, 8192, bar_a2);
+    uint8_t* a2 = sm + T_OFF_A2 + b * 32768;
+    bulk_load(a2, src, 16384, &bar_a2[b]);
+    bulk_load(a2 + 16384, src + 16384, 8192, &bar_a2[b]);
   };
 
   if (t == 0) {
-    mbar_init(bar_tma, 1);
-    mbar_init(bar_a2, 1);
-    mbar_init(bar_mma, 1);
+    for (int i = 0; i < 5; ++i) mbar_init(&bar_ld[i], 1);
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, kScanTmemCols);
-  // the lo half of [T_b; P] has no P rows: rows 64..127 stay zero
-  for (int i = t; i < 8192 / 16; i += kScanThreads)
-    reinterpret_cast<uint4*>(sm + S_OFF_A2_LO + 8192)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (warp == 0) tmem_alloc(tmem_slot, kScanTTmemCols);
+  // rows 64..127 of the lo part of [T_b; P] stay zero (P enters as hi only)
+  for (int i = t; i < 2 * 512; i += kScanTThreads) {
+    const int b = i >> 9, q = i & 511;
+    reinterpret_cast<uint4*>(sm + T_OFF_A2 + b * 32768 + 16384 + 8192)[q] =
+        make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + col0;
-  store_half_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, r, ch * 4, hrow);
+  const uint32_t lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+
+  auto write_s_operand = [&]() {
+    uint32_t hw[32], lw[32];
+    split_words<32>(S, hw, lw);
+    uint32_t a[16], b2[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) { a[i] = hw[i]; b2[i] = hw[16 + i]; }
+    tmem_st16(lane + TT_S + 32 * ch, a);
+    tmem_st16(lane + TT_S + 32 * ch + 16, b2);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) { a[i] = lw[i]; b2[i] = lw[16 + i]; }
+    tmem_st16(lane + TT_S + 64 + 32 * ch, a);
+    tmem_st16(lane + TT_S + 64 + 32 * ch + 16, b2);
+    tmem_st_wait();
+  };
+  write_s_operand();
 
   const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
   const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
+  const bool gate_thread = t >= kScanTGateBase && t < kScanTGateBase + kC;
   auto load_gates = [&](int64_t cs, float& ra, float& rb) {
-    if (t >= kGateBase && t < kGateBase + kC) {
-      const int64_t tok = cs + (t - kGateBase);
+    if (gate_thread) {
+      const int64_t tok = cs + (t - kScanTGateBase);
       const bool valid = tok < end;
       ra = valid ? load_scalar(p.a, p.a_dtype, tok * HV + h) : 0.0f;
       rb = valid ? load_scalar(p.b, p.b_dtype, tok * HV + h) : 0.0f;
     }
   };
-
-  uint32_t tma_phase = 0, a2_phase = 0, mma_phase = 0;
-  bool ok = true;
+  // gates of a chunk (warps 4-5): cumulative log decay, then gamma_j and f_j
+  auto gates = [&](float ra, float rb, int L, int buf) {
+    float* g = sG0 + buf * kC;
+    chunk_gates_w01(ra, rb, L, A_log, dtb, g, sBeta0 + buf * kC, kScanTGateBase);
+    named_bar_sync(1, 64);
+    const int j = t - kScanTGateBase;
+    sGam0[buf * kC + j] = ex2(g[j]);
+    sF0[buf * kC + j] = (j < L) ? ex2(g[kC - 1] - g[j]) : 0.0f;
+  };
   float ra = 0.f, rb = 0.f;
-  if (t == kIssuer) {
-    issue_tma(start);
-    issue_a2(0);
-  }
   load_gates(start, ra, rb);
-  if (t >= kGateBase && t < kGateBase + kC)
-    chunk_gates_w01(ra, rb, static_cast<int>((end - start) < kC ? (end - start) : kC), A_log,
-                    dtb, sG0, sBeta0, kGateBase);
-  __syncthreads();
+  if (gate_thread) gates(ra, rb, static_cast<int>((end - start) < kC ? (end - start) : kC), 0);
+  if (t == 0) issue_loads(start, 0, 0);
 
+  uint32_t mma_phase = 0;
+  bool ok = true;
   int64_t c = 0;
 #ifdef GDN_PHASE_PROFILE
   long long sphase_last_ = clock64();
@@ -445,156 +466,203 @@ __global__ void __launch_bounds__(kScanThreads, 2)
   for (int64_t cs = start; cs < end; cs += kC, ++c) {
     const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
     const int64_t next = cs + kC;
-    const int buf = static_cast<int>(c & 1);
-    const float* sG = sG0 + buf * kC;  // gates of this chunk (computed during the previous one)
-
-    // ---- [KH; QH] = [K;Q] H --------------------------------------------------------
-    SPHASE(0);  // loop top -> before TMA wait
-    ok = mbar_wait(bar_tma, tma_phase);
-    tma_phase ^= 1;
-    SPHASE(1);  // TMA wait
-    sync_before_mma();
-    if (!__syncthreads_and(ok)) break;
-    if (t == kIssuer) {
-      const Operand kq{smem_u32(sm + S_OFF_KQ), 0, false, 0, 0, 16384};
-      const Operand hB{smem_u32(sm + S_OFF_H_HI), smem_u32(sm + S_OFF_H_LO), true, 8192, 2048, 0};
-      issue_gemm(tmem + ST_1, kq, hB, ID_KM, 8);
-      mma_commit(bar_mma);
-    }
-    uint4 vraw[4];
-    if (r < kC) {
-      if (r < L) {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            p.v + ((cs + r) * HV + h) * kHeadDim + vt * kVT + col0);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) vraw[q] = src[q];
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) vraw[q] = make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
+    const int b = static_cast<int>(c & 1);
+    const uint32_t ph = static_cast<uint32_t>((c >> 1) & 1);
+    const float* sGam = sGam0 + b * kC;
+    const float* sF = sF0 + b * kC;
+    const uint8_t* kq = sm + T_OFF_KQ + b * 32768;
+    const uint8_t* a2 = sm + T_OFF_A2 + b * 32768;
+    const uint8_t* vt = sm + T_OFF_V + b * 16384;
     float nra = 0.f, nrb = 0.f;
     if (next < end) load_gates(next, nra, nrb);
-    SPHASE(2);  // G1 issue + V/gate loads
-    ok = mbar_wait(bar_mma, mma_phase);
-    mma_phase ^= 1;
+
+    SPHASE(0);  // top: next loads issued
+    // ---- D1 = S [K;Q]^T ---------------------------------------------------------------
+    ok = mbar_wait(&bar_ld[b], ph);
+    SPHASE(1);  // K/Q/V wait
+    tc_fence_before();
+    if (!__syncthreads_and(ok)) break;  // also: the S operand of every thread is stored
     tc_fence_after();
-    if (!__syncthreads_and(ok)) break;
-
-    const float g_last = sG[kC - 1];
-    if (r < kC) {
-      // X row j = r: V_j - gamma_j (K H)_j, into the dead Q half of the tile
-      float xr[32];
-      tmem_ld32w(trow + ST_1, xr);
-      const float gam = ex2(sG[r]);
+    if (t == 0) {
+      const uint64_t bd = desc_kmajor(smem_u32(kq));
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t w[4] = {vraw[q].x, vraw[q].y, vraw[q].z, vraw[q].w};
+      for (int s = 0; s < 8; ++s)
+        mma_bf16_ts(tmem + TT_D1, tmem + TT_S + s * 8,
+                    bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, s > 0);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          xr[q * 8 + 2 * e] = __uint_as_float(w[e] << 16) - gam * xr[q * 8 + 2 * e];
-          xr[q * 8 + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u) - gam * xr[q * 8 + 2 * e + 1];
-        }
-      }
-      store_half_row_split(sm + S_OFF_X_HI, sm + S_OFF_X_LO, r, ch * 4, xr);
-    }
-    SPHASE(3);  // G1 wait + X build
-
-    // ---- [U; O'] = [T_b; P] X ---------------------------------------------------------
-    ok = mbar_wait(bar_a2, a2_phase);
-    a2_phase ^= 1;
-    SPHASE(4);  // A2 wait
-    sync_before_mma();
-    if (!__syncthreads_and(ok)) break;
-    if (t == kIssuer) {
-      const Operand a2{smem_u32(sm + S_OFF_A2_HI), smem_u32(sm + S_OFF_A2_LO), false, 0, 0, 0};
-      const Operand xb{smem_u32(sm + S_OFF_X_HI), smem_u32(sm + S_OFF_X_LO), true, 8192, 2048, 0};
-      issue_gemm(tmem + ST_2, a2, xb, ID_KM, 4);
+      for (int s = 0; s < 8; ++s)
+        mma_bf16_ts(tmem + TT_D1, tmem + TT_S + 64 + s * 8,
+                    bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, 1);
       mma_commit(bar_mma);
+      // chunk c+1's tiles into the other buffers (their last users, chunk c-1, are done)
+      if (next < end) issue_loads(next, c + 1, b ^ 1);
     }
-    SPHASE(5);  // G2 issue
+    if (gate_thread && next < end)
+      gates(nra, nrb, static_cast<int>((end - next) < kC ? (end - next) : kC), b ^ 1);
+    SPHASE(2);  // sync + G1 issue + gates
     ok = mbar_wait(bar_mma, mma_phase);
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
-    if (t == kIssuer && next < end) issue_a2(c + 1);  // [T_b; P] of this chunk is consumed
-    if (r < kC) {
-      // f_j U_j with f_j = e^{Gamma_last - Gamma_j} (0 for padded rows): the state
-      // update then reads the raw K tile, dH = K^T diag(f) U
-      float u[32];
-      tmem_ld32w(trow + ST_2, u);
-      const float f = (r < L) ? ex2(g_last - sG[r]) : 0.0f;
-#pragma unroll
-      for (int v = 0; v < kHalf; ++v) u[v] *= f;
-      store_half_row_split(sm + S_OFF_X_HI, sm + S_OFF_X_LO, r, ch * 4, u);
-    }
-    SPHASE(6);  // G2 wait + U build
+    SPHASE(3);  // G1 wait
 
-    // ---- dH = K^T diag(f) U (into its own TMEM columns, so O' stays readable) -------------
-    sync_before_mma();
-    if (t == kIssuer) {
-      const Operand kt{smem_u32(sm + S_OFF_KQ), 0, true, 16384, 2048, 0};
-      const Operand ub{smem_u32(sm + S_OFF_X_HI), smem_u32(sm + S_OFF_X_LO), true, 8192, 2048, 0};
-      issue_gemm(tmem + ST_3, kt, ub, ID_MM, 4);
-      mma_commit(bar_mma);
-    }
-    // while the MMA runs: rows 64..127 produce the output, warps 0-1 the gates of the
-    // next chunk (into the other gate buffer)
-    if (r >= kC) {
-      const int i = r - kC;
-      float o[32], qhv[32];
-      tmem_ld32(trow + ST_2, o);
-      tmem_ld32(trow + ST_1, qhv);
-      tmem_ld_wait();
-      if (i < L) {
-        const float gam = ex2(sG[i]);
-        __nv_bfloat16* dst = p.out + ((cs + i) * HV + h) * kHeadDim + vt * kVT + col0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int v0 = q * 8 + 2 * e;
-            const float o0 = p.scale * fmaf(gam, qhv[v0], o[v0]);
-            const float o1 = p.scale * fmaf(gam, qhv[v0 + 1], o[v0 + 1]);
-            w[e] = pack2_rn(o0, o1);
-          }
-          *reinterpret_cast<uint4*>(dst + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-    } else if (t >= kGateBase && t < kGateBase + kC && next < end) {
-      const int nL = static_cast<int>((end - next) < kC ? (end - next) : kC);
-      chunk_gates_w01(nra, nrb, nL, A_log, dtb, sG0 + (buf ^ 1) * kC, sBeta0 + (buf ^ 1) * kC,
-                      kGateBase);
-    }
-    SPHASE(7);  // G3 issue + O + next gates
-    ok = mbar_wait(bar_mma, mma_phase);
-    mma_phase ^= 1;
-    tc_fence_after();
-    if (!__syncthreads_and(ok)) break;
-    SPHASE(8);  // G3 wait
-    if (t == kIssuer && next < end) issue_tma(next);
     {
-      // the fp32 state row stays in registers for the whole sequence
-      float dh[32];
-      tmem_ld32w(trow + ST_3, dh);
-      const float gl = ex2(g_last);
+      // X^T row v, columns j in [32c, 32c+32): V[j][v] - gamma_j (KH)^T[v][j]
+      float d[32];
+      tmem_ld32(lane + TT_D1 + 32 * ch, d);
+      tmem_ld_wait();
+      float x[32];
 #pragma unroll
-      for (int v = 0; v < kHalf; ++v) hrow[v] = fmaf(gl, hrow[v], dh[v]);
-      store_half_row_split(sm + S_OFF_H_HI, sm + S_OFF_H_LO, r, ch * 4, hrow);
+      for (int i = 0; i < 32; ++i) {
+        const int j = 32 * ch + i;
+        const unsigned short raw =
+            *reinterpret_cast<const unsigned short*>(vt + j * 256 + v * 2);
+        x[i] = __uint_as_float(static_cast<uint32_t>(raw) << 16) - sGam[j] * d[i];
+      }
+      uint32_t hw[16], lw[16];
+      split_words<16>(x, hw, lw);
+      tmem_st16(lane + TT_X + 16 * ch, hw);
+      tmem_st16(lane + TT_X + 32 + 16 * ch, lw);
+      tmem_st_wait();
     }
-    SPHASE(9);  // H update
+
+    SPHASE(4);  // X build
+    // ---- D2 = X^T [T_b; P]^T -----------------------------------------------------------
+    ok = mbar_wait(&bar_a2[b], ph);
+    tc_fence_before();
+    if (!__syncthreads_and(ok)) break;
+    tc_fence_after();
+    if (t == 0) {
+      const uint64_t bh = desc_kmajor(smem_u32(a2)), bl = desc_kmajor(smem_u32(a2 + 16384));
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + s * 8, bh + ((s * 32) >> 4), ID_T_K, s > 0);
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K, 1);
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + s * 8, bl + ((s * 32) >> 4), ID_T_K, 1);
+      mma_commit(bar_mma);
+    }
+    SPHASE(5);  // A2 wait + sync + G2 issue
+    ok = mbar_wait(bar_mma, mma_phase);
+    mma_phase ^= 1;
+    tc_fence_after();
+    if (!__syncthreads_and(ok)) break;
+    SPHASE(6);  // G2 wait
+    {
+      // U'^T = U^T diag(f) -> operand (over X^T, consumed)
+      float u[32];
+      tmem_ld32(lane + TT_D2 + 32 * ch, u);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) u[i] *= sF[32 * ch + i];
+      uint32_t hw[16], lw[16];
+      split_words<16>(u, hw, lw);
+      tmem_st16(lane + TT_X + 16 * ch, hw);
+      tmem_st16(lane + TT_X + 32 + 16 * ch, lw);
+      tmem_st_wait();
+    }
+    SPHASE(7);  // U' + O
+    // ---- dS = U'^T K (into the S operand columns: G1 is done) ---------------------------
+    if (t == 0) bulk_wait_read<1>();  // this chunk's output tile buffer is free again
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (t == 0) {
+      const uint64_t bk = desc_mnmajor(smem_u32(kq), 16384);
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        mma_bf16_ts(tmem + TT_S, tmem + TT_X + s * 8, bk + ((s * 2048) >> 4), ID_T_MN, s > 0);
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        mma_bf16_ts(tmem + TT_S, tmem + TT_X + 32 + s * 8, bk + ((s * 2048) >> 4), ID_T_MN, 1);
+      mma_commit(bar_mma);
+    }
+    {
+      // while dS is computed: O^T row v, tokens i in [32c, 32c+32) (D1 and D2 columns
+      // that the state-update MMA does not touch)
+      float o[32], qv[32];
+      tmem_ld32(lane + TT_D2 + 64 + 32 * ch, o);
+      tmem_ld32(lane + TT_D1 + 64 + 32 * ch, qv);
+      tmem_ld_wait();
+      if (L == kC) {
+        // full chunk: stage the tile, one TMA store after the next barrier
+        __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(sm + T_OFF_O + b * 16384);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int ii = 32 * ch + i;
+          tile[ii * kHeadDim + v] = __float2bfloat16_rn(p.scale * fmaf(sGam[ii], qv[i], o[i]));
+        }
+      } else {
+        // partial (last) chunk: only its own tokens; rows past L belong to the next sequence
+        __nv_bfloat16* dst = p.out + (cs * HV + h) * kHeadDim + v;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int ii = 32 * ch + i;
+          if (ii < L)
+            dst[static_cast<int64_t>(ii) * HV * kHeadDim] =
+                __float2bfloat16_rn(p.scale * fmaf(sGam[ii], qv[i], o[i]));
+        }
+      }
+      fence_async_smem();
+    }
+    ok = mbar_wait(bar_mma, mma_phase);
+    mma_phase ^= 1;
+    tc_fence_after();
+    if (!__syncthreads_and(ok)) break;
+    SPHASE(8);  // sync + G3 issue + O + wait
+    {
+      float d0[32], d1[32];
+      tmem_ld32(lane + TT_S + 64 * ch, d0);
+      tmem_ld32(lane + TT_S + 64 * ch + 32, d1);
+      tmem_ld_wait();
+      const float gl = sGam[kC - 1];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        S[i] = fmaf(gl, S[i], d0[i]);
+        S[32 + i] = fmaf(gl, S[32 + i], d1[i]);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // every thread has read its dS columns before they are overwritten
+    tc_fence_after();
+    if (t == 0 && L == kC) {
+      tma_store_3d(&maps.o, sm + T_OFF_O + b * 16384, 0, h, static_cast<int>(cs));
+      bulk_commit();
+    }
+    write_s_operand();
+    SPHASE(9);  // S update + operand
   }
 
+  if (t == 0) bulk_wait_all();  // output stores complete before the block exits
   if (ok) {
 #pragma unroll
-    for (int v = 0; v < kHalf; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
-  } else if (t == kIssuer && p.status) {
+    for (int i = 0; i < 64; i += 4)
+      *reinterpret_cast<float4*>(p.new_state + sbase + i) =
+          make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
+  } else if (t == 0 && p.status) {
     atomicExch(p.status, 1);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, kScanTmemCols);
+  if (warp == 0) tmem_dealloc(tmem, kScanTTmemCols);
+}
+
+bool encode_v_map(CUtensorMap* map, const void* base, int64_t T, int HV) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(HV),
+                              static_cast<cuuint64_t>(T)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHeadDim) * 2,
+                                 static_cast<cuuint64_t>(HV) * kHeadDim * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kHeadDim), 1, kC};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -625,9 +693,7 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   const void* qb = p.T > 0 ? static_cast<const void*>(p.q) : static_cast<const void*>(p.new_state);
   if (!encode_qk_map(&maps.k, kb, Tm, p.HQ) || !encode_qk_map(&maps.q, qb, Tm, p.HQ)) return -2;
   if (cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
-          cudaSuccess ||
-      cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem) !=
-          cudaSuccess)
+      cudaSuccess)
     return -1;
   chunk_offsets_kernel<<<1, 1024, 0, stream>>>(p, offs);
   scan_order_kernel<<<static_cast<unsigned>((p.N + 255) / 256), 256, 0, stream>>>(p.N, offs,
@@ -636,9 +702,17 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   if (p.T > 0) {
     prep_kernel<<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(p, maps, offs, a2);
   }
-  scan_kernel<<<static_cast<unsigned>(p.N * p.HV * kTiles), kScanThreads, kScanSmem, stream>>>(p, maps,
-                                                                                     offs, order,
-                                                                                     a2);
+  ScanMaps smaps;
+  smaps.k = maps.k;
+  smaps.q = maps.q;
+  const void* vb = p.T > 0 ? static_cast<const void*>(p.v) : static_cast<const void*>(p.new_state);
+  void* ob = p.T > 0 ? static_cast<void*>(p.out) : static_cast<void*>(p.new_state);
+  if (!encode_v_map(&smaps.v, vb, Tm, p.HV) || !encode_v_map(&smaps.o, ob, Tm, p.HV)) return -2;
+  if (cudaFuncSetAttribute(scan_t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kScanTSmem) != cudaSuccess)
+    return -1;
+  scan_t_kernel<<<static_cast<unsigned>(p.N * p.HV), kScanTThreads, kScanTSmem, stream>>>(
+      p, smaps, offs, order, a2);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
