@@ -301,8 +301,8 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
 //   D2 = X^T [T_b; P]^T   -> [ U^T | (P X)^T ]
 //   U'^T = U^T diag(f);  O^T = scale ((QH)^T diag(gamma) + (P X)^T)
 //   dS = U'^T K;  S <- gamma_last S + dS                   (S = H^T, k-last, in registers)
-// Thread t owns state row v = t % 128 and half c = t / 128 of every row-sliced
-// quantity (k in [64c, 64c+64) of S; j in [32c, 32c+32) of X, U; i likewise of O).
+// Thread t owns state row v = t % 128 and quarter c = t / 128 of every row-sliced
+// quantity (k in [32c, 32c+32) of S; j in [16c, 16c+16) of X, U; i likewise of O).
 // K/Q, V and [T_b; P] are double-buffered: chunk c+1's tiles are requested when
 // chunk c starts.
 constexpr uint32_t T_OFF_KQ = 0;          // 2 x 32 KB
@@ -322,7 +322,7 @@ constexpr uint32_t TT_X = 256;  // X^T then U'^T operand: hi [256, 288) | lo [28
 constexpr uint32_t TT_D2 = 320; // 128 fp32 columns
 constexpr uint32_t ID_T_K = idesc_bf16(128, 128, false, false);   // B K-major
 constexpr uint32_t ID_T_MN = idesc_bf16(128, 128, false, true);   // B MN-major
-constexpr int kScanTThreads = 256;
+constexpr int kScanTThreads = 512;
 constexpr int kScanTGateBase = 128;  // warps 4-5 compute the next chunk's gates
 
 struct ScanMaps {
@@ -361,18 +361,18 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
   int64_t start, end;
   seq_bounds(p, n, start, end);
 
-  // this thread's half of state row v: S[n, h, v, 64c .. 64c+64)
-  const int64_t sbase = ((n * HV + h) * kHeadDim + v) * kHeadDim + 64 * ch;
-  float S[64];
+  // this thread's quarter of state row v: S[n, h, v, 32c .. 32c+32)
+  const int64_t sbase = ((n * HV + h) * kHeadDim + v) * kHeadDim + 32 * ch;
+  float S[32];
 #pragma unroll
-  for (int i = 0; i < 64; i += 4) {
+  for (int i = 0; i < 32; i += 4) {
     const float4 x = p.state ? *reinterpret_cast<const float4*>(p.state + sbase + i)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
     S[i] = x.x; S[i + 1] = x.y; S[i + 2] = x.z; S[i + 3] = x.w;
   }
   if (end <= start) {  // empty sequence: pass the state through
 #pragma unroll
-    for (int i = 0; i < 64; i += 4)
+    for (int i = 0; i < 32; i += 4)
       *reinterpret_cast<float4*>(p.new_state + sbase + i) =
           make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
     return;
@@ -417,17 +417,10 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
   const uint32_t lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 
   auto write_s_operand = [&]() {
-    uint32_t hw[32], lw[32];
-    split_words<32>(S, hw, lw);
-    uint32_t a[16], b2[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) { a[i] = hw[i]; b2[i] = hw[16 + i]; }
-    tmem_st16(lane + TT_S + 32 * ch, a);
-    tmem_st16(lane + TT_S + 32 * ch + 16, b2);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) { a[i] = lw[i]; b2[i] = lw[16 + i]; }
-    tmem_st16(lane + TT_S + 64 + 32 * ch, a);
-    tmem_st16(lane + TT_S + 64 + 32 * ch + 16, b2);
+    uint32_t hw[16], lw[16];
+    split_words<16>(S, hw, lw);
+    tmem_st16(lane + TT_S + 16 * ch, hw);
+    tmem_st16(lane + TT_S + 64 + 16 * ch, lw);
     tmem_st_wait();
   };
   write_s_operand();
@@ -507,22 +500,22 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
     SPHASE(3);  // G1 wait
 
     {
-      // X^T row v, columns j in [32c, 32c+32): V[j][v] - gamma_j (KH)^T[v][j]
-      float d[32];
-      tmem_ld32(lane + TT_D1 + 32 * ch, d);
+      // X^T row v, columns j in [16c, 16c+16): V[j][v] - gamma_j (KH)^T[v][j]
+      float d[16];
+      tmem_ld16(lane + TT_D1 + 16 * ch, d);
       tmem_ld_wait();
-      float x[32];
+      float x[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int j = 32 * ch + i;
+      for (int i = 0; i < 16; ++i) {
+        const int j = 16 * ch + i;
         const unsigned short raw =
             *reinterpret_cast<const unsigned short*>(vt + j * 256 + v * 2);
         x[i] = __uint_as_float(static_cast<uint32_t>(raw) << 16) - sGam[j] * d[i];
       }
-      uint32_t hw[16], lw[16];
-      split_words<16>(x, hw, lw);
-      tmem_st16(lane + TT_X + 16 * ch, hw);
-      tmem_st16(lane + TT_X + 32 + 16 * ch, lw);
+      uint32_t hw[8], lw[8];
+      split_words<8>(x, hw, lw);
+      tmem_st8(lane + TT_X + 8 * ch, hw);
+      tmem_st8(lane + TT_X + 32 + 8 * ch, lw);
       tmem_st_wait();
     }
 
@@ -553,15 +546,15 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
     SPHASE(6);  // G2 wait
     {
       // U'^T = U^T diag(f) -> operand (over X^T, consumed)
-      float u[32];
-      tmem_ld32(lane + TT_D2 + 32 * ch, u);
+      float u[16];
+      tmem_ld16(lane + TT_D2 + 16 * ch, u);
       tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) u[i] *= sF[32 * ch + i];
-      uint32_t hw[16], lw[16];
-      split_words<16>(u, hw, lw);
-      tmem_st16(lane + TT_X + 16 * ch, hw);
-      tmem_st16(lane + TT_X + 32 + 16 * ch, lw);
+      for (int i = 0; i < 16; ++i) u[i] *= sF[16 * ch + i];
+      uint32_t hw[8], lw[8];
+      split_words<8>(u, hw, lw);
+      tmem_st8(lane + TT_X + 8 * ch, hw);
+      tmem_st8(lane + TT_X + 32 + 8 * ch, lw);
       tmem_st_wait();
     }
     SPHASE(7);  // U' + O
@@ -583,24 +576,24 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
     {
       // while dS is computed: O^T row v, tokens i in [32c, 32c+32) (D1 and D2 columns
       // that the state-update MMA does not touch)
-      float o[32], qv[32];
-      tmem_ld32(lane + TT_D2 + 64 + 32 * ch, o);
-      tmem_ld32(lane + TT_D1 + 64 + 32 * ch, qv);
+      float o[16], qv[16];
+      tmem_ld16(lane + TT_D2 + 64 + 16 * ch, o);
+      tmem_ld16(lane + TT_D1 + 64 + 16 * ch, qv);
       tmem_ld_wait();
       if (L == kC) {
         // full chunk: stage the tile, one TMA store after the next barrier
         __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(sm + T_OFF_O + b * 16384);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int ii = 32 * ch + i;
+        for (int i = 0; i < 16; ++i) {
+          const int ii = 16 * ch + i;
           tile[ii * kHeadDim + v] = __float2bfloat16_rn(p.scale * fmaf(sGam[ii], qv[i], o[i]));
         }
       } else {
         // partial (last) chunk: only its own tokens; rows past L belong to the next sequence
         __nv_bfloat16* dst = p.out + (cs * HV + h) * kHeadDim + v;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int ii = 32 * ch + i;
+        for (int i = 0; i < 16; ++i) {
+          const int ii = 16 * ch + i;
           if (ii < L)
             dst[static_cast<int64_t>(ii) * HV * kHeadDim] =
                 __float2bfloat16_rn(p.scale * fmaf(sGam[ii], qv[i], o[i]));
@@ -614,16 +607,12 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
     if (!__syncthreads_and(ok)) break;
     SPHASE(8);  // sync + G3 issue + O + wait
     {
-      float d0[32], d1[32];
-      tmem_ld32(lane + TT_S + 64 * ch, d0);
-      tmem_ld32(lane + TT_S + 64 * ch + 32, d1);
+      float d0[32];
+      tmem_ld32(lane + TT_S + 32 * ch, d0);
       tmem_ld_wait();
       const float gl = sGam[kC - 1];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        S[i] = fmaf(gl, S[i], d0[i]);
-        S[32 + i] = fmaf(gl, S[32 + i], d1[i]);
-      }
+      for (int i = 0; i < 32; ++i) S[i] = fmaf(gl, S[i], d0[i]);
     }
     tc_fence_before();
     __syncthreads();  // every thread has read its dS columns before they are overwritten
@@ -639,7 +628,7 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
   if (t == 0) bulk_wait_all();  // output stores complete before the block exits
   if (ok) {
 #pragma unroll
-    for (int i = 0; i < 64; i += 4)
+    for (int i = 0; i < 32; i += 4)
       *reinterpret_cast<float4*>(p.new_state + sbase + i) =
           make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
   } else if (t == 0 && p.status) {
