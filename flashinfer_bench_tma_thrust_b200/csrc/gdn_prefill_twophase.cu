@@ -487,9 +487,10 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
         mma_bf16_ts(tmem + TT_D1, tmem + TT_S + 64 + s * 8,
                     bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, 1);
       mma_commit(bar_mma);
-      // chunk c+1's tiles into the other buffers (their last users, chunk c-1, are done)
-      if (next < end) issue_loads(next, c + 1, b ^ 1);
     }
+    // chunk c+1's tiles into the other buffers (their last users, chunk c-1, are done),
+    // from another warp while thread 0 is blocked issuing the MMAs
+    if (t == 32 && next < end) issue_loads(next, c + 1, b ^ 1);
     if (gate_thread && next < end)
       gates(nra, nrb, static_cast<int>((end - next) < kC ? (end - next) : kC), b ^ 1);
     SPHASE(2);  // sync + G1 issue + gates
