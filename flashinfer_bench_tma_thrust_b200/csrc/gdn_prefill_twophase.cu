@@ -322,6 +322,9 @@ constexpr uint32_t TT_X = 256;  // X^T then U'^T operand: hi [256, 288) | lo [28
 constexpr uint32_t TT_D2 = 320; // 128 fp32 columns
 constexpr uint32_t ID_T_K = idesc_bf16(128, 128, false, false);   // B K-major
 constexpr uint32_t ID_T_MN = idesc_bf16(128, 128, false, true);   // B MN-major
+// N = 64: the lo (correction) terms are taken only for the columns that feed the state
+// (KH and U); the QH and PX columns reach the bf16 output alone and take hi x hi
+constexpr uint32_t ID_T_K64 = idesc_bf16(128, 64, false, false);
 constexpr int kScanTThreads = 512;
 constexpr int kScanTGateBase = 128;  // warps 4-5 compute the next chunk's gates
 
@@ -476,6 +479,7 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
     tc_fence_before();
     if (!__syncthreads_and(ok)) break;  // also: the S operand of every thread is stored
     tc_fence_after();
+    SPHASE(10);  // top barrier
     if (t == 0) {
       const uint64_t bd = desc_kmajor(smem_u32(kq));
 #pragma unroll
@@ -485,7 +489,7 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
 #pragma unroll
       for (int s = 0; s < 8; ++s)
         mma_bf16_ts(tmem + TT_D1, tmem + TT_S + 64 + s * 8,
-                    bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, 1);
+                    bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K64, 1);
       mma_commit(bar_mma);
     }
     // chunk c+1's tiles into the other buffers (their last users, chunk c-1, are done),
@@ -533,10 +537,10 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
         mma_bf16_ts(tmem + TT_D2, tmem + TT_X + s * 8, bh + ((s * 32) >> 4), ID_T_K, s > 0);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K, 1);
+        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K64, 1);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + s * 8, bl + ((s * 32) >> 4), ID_T_K, 1);
+        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + s * 8, bl + ((s * 32) >> 4), ID_T_K64, 1);
       mma_commit(bar_mma);
     }
     SPHASE(5);  // A2 wait + sync + G2 issue
