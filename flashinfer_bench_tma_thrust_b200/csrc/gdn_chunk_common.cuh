@@ -397,10 +397,10 @@ __device__ __forceinline__ void build_a_m_256(uint32_t ts_row, float* sAf, const
   }
 }
 
-// solve_tb for 256 threads (8 warps), written for instruction count (the prep
-// kernel runs three blocks per SM and is issue-bound): diagonal blocks by
-// right-looking substitution (each step's updates are independent), off-diagonal
-// blocks one warp per block with 8 outputs per lane and float4 loads.
+// solve_tb for 256 threads (8 warps): the 16 x 16 diagonal blocks by right-looking
+// substitution (each step's updates are independent), then the off-diagonal blocks
+// in two levels of the block-diagonal inverse formula (16 -> 32, 32 -> 64), each
+// spread over all 8 warps so that the dependent chain is short.
 template <class Lay>
 __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float* sBeta,
                                              uint8_t* tb_hi, uint8_t* tb_lo) {
@@ -418,54 +418,70 @@ __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float
     }
 #pragma unroll
     for (int i = 0; i < 16; ++i) sTf[Lay::idx(b0 + i, b0 + lane)] = x[i];
+  } else if (warp >= 4 && warp < 6) {
+    // block (0, 1) of T must read as zero in the level-2 product below
+    const int q = t - 128, row = q >> 2, col = 16 + (q & 3) * 4;
+    *reinterpret_cast<float4*>(sTf + Lay::idx(row, col)) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   __syncthreads();
-  const int r = lane >> 1, c0 = (lane & 1) * 8;
-  for (int d = 1; d < 4; ++d) {
-    if (warp < 4 - d) {
-      const int I = d + warp, J = warp;
-      float w[8];
+  // Two levels, every warp busy at each (T_IJ = -T_II A_IJ T_JJ for the lower blocks
+  // of a block-diagonal inverse):
+  // level 1, 16 -> 32: blocks (1,0) [warps 0-3] and (3,2) [warps 4-7]; 2 outputs per
+  // thread (row r, columns c0, c0+1); scratch W in block (0, 2 + g).
+  {
+    const int g = warp >> 2, q = t & 127, r = q >> 3, c0 = (q & 7) * 2;
+    const int I = 2 * g + 1, J = 2 * g;
+    float w0 = 0.f, w1 = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) w[e] = 0.f;
-      for (int K = J; K < I; ++K) {  // W_IJ = sum_K A_IK T_KJ
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float a = sAf[Lay::idx(16 * I + r, 16 * K + k)];
-          const float4 t0 = *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * K + k, 16 * J + c0));
-          const float4 t1 =
-              *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * K + k, 16 * J + c0 + 4));
-          w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
-          w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
-          w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
-          w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
-        }
-      }
-      // scratch block (J, I)
-      *reinterpret_cast<float4*>(sTf + Lay::idx(16 * J + r, 16 * I + c0)) =
-          make_float4(w[0], w[1], w[2], w[3]);
-      *reinterpret_cast<float4*>(sTf + Lay::idx(16 * J + r, 16 * I + c0 + 4)) =
-          make_float4(w[4], w[5], w[6], w[7]);
-      __syncwarp();
-#pragma unroll
-      for (int e = 0; e < 8; ++e) w[e] = 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {  // T_IJ = -T_II W_IJ
-        const float a = sTf[Lay::idx(16 * I + r, 16 * I + k)];
-        const float4 t0 = *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * J + k, 16 * I + c0));
-        const float4 t1 =
-            *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * J + k, 16 * I + c0 + 4));
-        w[0] = fmaf(a, t0.x, w[0]); w[1] = fmaf(a, t0.y, w[1]);
-        w[2] = fmaf(a, t0.z, w[2]); w[3] = fmaf(a, t0.w, w[3]);
-        w[4] = fmaf(a, t1.x, w[4]); w[5] = fmaf(a, t1.y, w[5]);
-        w[6] = fmaf(a, t1.z, w[6]); w[7] = fmaf(a, t1.w, w[7]);
-      }
-      *reinterpret_cast<float4*>(sTf + Lay::idx(16 * I + r, 16 * J + c0)) =
-          make_float4(-w[0], -w[1], -w[2], -w[3]);
-      *reinterpret_cast<float4*>(sTf + Lay::idx(16 * I + r, 16 * J + c0 + 4)) =
-          make_float4(-w[4], -w[5], -w[6], -w[7]);
+    for (int k = 0; k < 16; ++k) {
+      const float a = sAf[Lay::idx(16 * I + r, 16 * J + k)];
+      const float2 tv = *reinterpret_cast<const float2*>(sTf + Lay::idx(16 * J + k, 16 * J + c0));
+      w0 = fmaf(a, tv.x, w0);
+      w1 = fmaf(a, tv.y, w1);
     }
-    __syncthreads();
+    *reinterpret_cast<float2*>(sTf + Lay::idx(r, 32 + 16 * g + c0)) = make_float2(w0, w1);
+    named_bar_sync(2 + g, 128);
+    // T_II is lower triangular: rows r of this warp need k <= r only
+    const int kmax = 4 * (warp & 3) + 4;
+    float v0 = 0.f, v1 = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < kmax; ++k) {
+      const float a = sTf[Lay::idx(16 * I + r, 16 * I + k)];
+      const float2 wv = *reinterpret_cast<const float2*>(sTf + Lay::idx(k, 32 + 16 * g + c0));
+      v0 = fmaf(a, wv.x, v0);
+      v1 = fmaf(a, wv.y, v1);
+    }
+    *reinterpret_cast<float2*>(sTf + Lay::idx(16 * I + r, 16 * J + c0)) = make_float2(-v0, -v1);
   }
+  __syncthreads();
+  // level 2, 32 -> 64: block rows 32..63 x cols 0..31, 4 outputs per thread; scratch W
+  // in rows 0..31 x cols 32..63 (the level-1 scratch is consumed)
+  {
+    const int r = t >> 3, c0 = (t & 7) * 4;
+    float w[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float a = sAf[Lay::idx(32 + r, k)];
+      const float4 tv = *reinterpret_cast<const float4*>(sTf + Lay::idx(k, c0));
+      w[0] = fmaf(a, tv.x, w[0]); w[1] = fmaf(a, tv.y, w[1]);
+      w[2] = fmaf(a, tv.z, w[2]); w[3] = fmaf(a, tv.w, w[3]);
+    }
+    *reinterpret_cast<float4*>(sTf + Lay::idx(r, 32 + c0)) = make_float4(w[0], w[1], w[2], w[3]);
+    __syncthreads();
+    // T_{[32,64)} is lower triangular: rows of warp w (4w .. 4w+3) need k < 4w + 4
+    const int kmax = 4 * warp + 4;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int k = 0; k < kmax; ++k) {
+      const float a = sTf[Lay::idx(32 + r, 32 + k)];
+      const float4 wv = *reinterpret_cast<const float4*>(sTf + Lay::idx(k, 32 + c0));
+      v[0] = fmaf(a, wv.x, v[0]); v[1] = fmaf(a, wv.y, v[1]);
+      v[2] = fmaf(a, wv.z, v[2]); v[3] = fmaf(a, wv.w, v[3]);
+    }
+    *reinterpret_cast<float4*>(sTf + Lay::idx(32 + r, c0)) =
+        make_float4(-v[0], -v[1], -v[2], -v[3]);
+  }
+  __syncthreads();
   {
     // T_b = T diag(beta), MN-major rows j x cols n: a quarter row (2 chunks) per thread
     const int j = t & (kC - 1), qq = t >> 6;

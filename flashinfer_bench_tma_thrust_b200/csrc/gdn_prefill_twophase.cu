@@ -480,17 +480,18 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
     if (!__syncthreads_and(ok)) break;  // also: the S operand of every thread is stored
     tc_fence_after();
     SPHASE(10);  // top barrier
-    if (t == 0) {
+    if (warp == 0) {
+      __syncwarp();
       const uint64_t bd = desc_kmajor(smem_u32(kq));
 #pragma unroll
       for (int s = 0; s < 8; ++s)
-        mma_bf16_ts(tmem + TT_D1, tmem + TT_S + s * 8,
+        mma_bf16_ts_w(tmem + TT_D1, tmem + TT_S + s * 8,
                     bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, s > 0);
 #pragma unroll
       for (int s = 0; s < 8; ++s)
-        mma_bf16_ts(tmem + TT_D1, tmem + TT_S + 64 + s * 8,
+        mma_bf16_ts_w(tmem + TT_D1, tmem + TT_S + 64 + s * 8,
                     bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K64, 1);
-      mma_commit(bar_mma);
+      mma_commit_w(bar_mma);
     }
     // chunk c+1's tiles into the other buffers (their last users, chunk c-1, are done),
     // from another warp while thread 0 is blocked issuing the MMAs
@@ -530,18 +531,19 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
     tc_fence_before();
     if (!__syncthreads_and(ok)) break;
     tc_fence_after();
-    if (t == 0) {
+    if (warp == 0) {
+      __syncwarp();
       const uint64_t bh = desc_kmajor(smem_u32(a2)), bl = desc_kmajor(smem_u32(a2 + 16384));
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + s * 8, bh + ((s * 32) >> 4), ID_T_K, s > 0);
+        mma_bf16_ts_w(tmem + TT_D2, tmem + TT_X + s * 8, bh + ((s * 32) >> 4), ID_T_K, s > 0);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K64, 1);
+        mma_bf16_ts_w(tmem + TT_D2, tmem + TT_X + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K64, 1);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        mma_bf16_ts(tmem + TT_D2, tmem + TT_X + s * 8, bl + ((s * 32) >> 4), ID_T_K64, 1);
-      mma_commit(bar_mma);
+        mma_bf16_ts_w(tmem + TT_D2, tmem + TT_X + s * 8, bl + ((s * 32) >> 4), ID_T_K64, 1);
+      mma_commit_w(bar_mma);
     }
     SPHASE(5);  // A2 wait + sync + G2 issue
     ok = mbar_wait(bar_mma, mma_phase);
@@ -568,15 +570,16 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (t == 0) {
+    if (warp == 0) {
+      __syncwarp();
       const uint64_t bk = desc_mnmajor(smem_u32(kq), 16384);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        mma_bf16_ts(tmem + TT_S, tmem + TT_X + s * 8, bk + ((s * 2048) >> 4), ID_T_MN, s > 0);
+        mma_bf16_ts_w(tmem + TT_S, tmem + TT_X + s * 8, bk + ((s * 2048) >> 4), ID_T_MN, s > 0);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        mma_bf16_ts(tmem + TT_S, tmem + TT_X + 32 + s * 8, bk + ((s * 2048) >> 4), ID_T_MN, 1);
-      mma_commit(bar_mma);
+        mma_bf16_ts_w(tmem + TT_S, tmem + TT_X + 32 + s * 8, bk + ((s * 2048) >> 4), ID_T_MN, 1);
+      mma_commit_w(bar_mma);
     }
     {
       // while dS is computed: O^T row v, tokens i in [32c, 32c+32) (D1 and D2 columns
