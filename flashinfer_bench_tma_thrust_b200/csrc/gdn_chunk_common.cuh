@@ -94,6 +94,7 @@ __device__ __forceinline__ void sync_before_mma() {
 
 // Issue `ksteps` MMAs of the three-term split product (hi*hi + hi*lo + lo*hi)
 // or of a plain product when a_lo == 0 and b_lo == 0 (exact bf16 operands).
+// Called by all lanes of one warp (warp-level MMA issue; see mma_bf16_w).
 struct Operand {
   uint32_t hi, lo;   // shared addresses of the two halves (lo == 0: exact, no second half)
   bool mn;           // MN-major
@@ -119,14 +120,14 @@ __device__ __forceinline__ void issue_gemm(uint32_t d, const Operand& a, const O
   const uint64_t ah = op_desc(a, a.hi, 0), bh = op_desc(b, b.hi, 0);
   const uint64_t al = a.lo ? op_desc(a, a.lo, 0) : 0, bl = b.lo ? op_desc(b, b.lo, 0) : 0;
 #pragma unroll
-  for (int s = 0; s < ksteps; ++s) mma_bf16(d, ah + op_step(a, s), bh + op_step(b, s), idesc, s > 0);
+  for (int s = 0; s < ksteps; ++s) mma_bf16_w(d, ah + op_step(a, s), bh + op_step(b, s), idesc, s > 0);
   if (b.lo) {
 #pragma unroll
-    for (int s = 0; s < ksteps; ++s) mma_bf16(d, ah + op_step(a, s), bl + op_step(b, s), idesc, 1);
+    for (int s = 0; s < ksteps; ++s) mma_bf16_w(d, ah + op_step(a, s), bl + op_step(b, s), idesc, 1);
   }
   if (a.lo) {
 #pragma unroll
-    for (int s = 0; s < ksteps; ++s) mma_bf16(d, al + op_step(a, s), bh + op_step(b, s), idesc, 1);
+    for (int s = 0; s < ksteps; ++s) mma_bf16_w(d, al + op_step(a, s), bh + op_step(b, s), idesc, 1);
   }
 }
 

@@ -193,12 +193,12 @@ __global__ void __launch_bounds__(128, 2)
     sync_before_mma();
     if (!__syncthreads_and(ok)) break;
     PHASE(1);  // TMA wait
-    if (t == 0) {
+    if (t < 32) {  // warp 0 issues
       const Operand kq{smem_u32(sm + OFF_KQ), 0, false, 0, 0, 16384};
       const Operand hB{smem_u32(sm + OFF_H_HI), smem_u32(sm + OFF_H_LO), true, 8192, 2048, 0};
       issue_gemm(tmem + TM_S, kq, kq, ID_KK, 8);
       issue_gemm(tmem + TM_1, kq, hB, ID_KM, 8);
-      mma_commit(bar_mma);
+      mma_commit_w(bar_mma);
     }
     // V row of this thread's token (independent of the MMAs; latency overlaps them)
     uint4 vraw[8];
@@ -247,11 +247,11 @@ __global__ void __launch_bounds__(128, 2)
     PHASE(6);  // T_b write
     // ---- [T_b; P] = [I; M] T_b -----------------------------------------------------
     sync_before_mma();
-    if (t == 0) {
+    if (t < 32) {  // warp 0 issues
       const Operand a2{smem_u32(sm + OFF_A2_HI), smem_u32(sm + OFF_A2_LO), false, 0, 0, 0};
       const Operand tb{smem_u32(sm + OFF_TB_HI), smem_u32(sm + OFF_TB_LO), true, 8192, 2048, 0};
       issue_gemm(tmem + TM_S, a2, tb, ID_KM, 4);
-      mma_commit(bar_mma);
+      mma_commit_w(bar_mma);
     }
     ok = mbar_wait(bar_mma, mma_phase);
     mma_phase ^= 1;
@@ -267,11 +267,11 @@ __global__ void __launch_bounds__(128, 2)
     PHASE(8);  // A2 write
     // ---- [U; O'] = [T_b; P] X ----------------------------------------------------------
     sync_before_mma();
-    if (t == 0) {
+    if (t < 32) {  // warp 0 issues
       const Operand a2{smem_u32(sm + OFF_A2_HI), smem_u32(sm + OFF_A2_LO), false, 0, 0, 0};
       const Operand xb{smem_u32(sm + OFF_X_HI), smem_u32(sm + OFF_X_LO), true, 8192, 2048, 0};
       issue_gemm(tmem + TM_2, a2, xb, ID_KM, 4);
-      mma_commit(bar_mma);
+      mma_commit_w(bar_mma);
     }
     ok = mbar_wait(bar_mma, mma_phase);
     mma_phase ^= 1;
@@ -313,11 +313,11 @@ __global__ void __launch_bounds__(128, 2)
     PHASE(10);  // U / O
     // ---- dH = K^T diag(f) U;  H <- gamma_last H + dH ----------------------------------------
     sync_before_mma();
-    if (t == 0) {
+    if (t < 32) {  // warp 0 issues
       const Operand kt{smem_u32(sm + OFF_KQ), 0, true, 16384, 2048, 0};
       const Operand ub{smem_u32(sm + OFF_X_HI), smem_u32(sm + OFF_X_LO), true, 8192, 2048, 0};
       issue_gemm(tmem + TM_2, kt, ub, ID_MM, 4);
-      mma_commit(bar_mma);
+      mma_commit_w(bar_mma);
     }
     ok = mbar_wait(bar_mma, mma_phase);
     mma_phase ^= 1;

@@ -228,10 +228,10 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
   PPHASE(1);  // TMA wait
   sync_before_mma();
   if (__syncthreads_and(ok)) {
-    if (t == 0) {
+    if (t < 32) {  // warp 0 issues
       const Operand kq{smem_u32(sm + P_OFF_KQ), 0, false, 0, 0, 16384};
       issue_gemm(tmem + PT_S, kq, kq, ID_KK, 8);
-      mma_commit(bar_mma);
+      mma_commit_w(bar_mma);
     }
     ok = mbar_wait(bar_mma, 0);
     tc_fence_after();
@@ -244,12 +244,12 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
       solve_tb_256<PadLayout>(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
       PPHASE(4);  // solve + T_b
       sync_before_mma();
-      if (t == 0) {  // P = M T_b (result rows 0..63)
+      if (t < 32) {  // warp 0 issues  // P = M T_b (result rows 0..63)
         const Operand mA{smem_u32(sm + P_OFF_M_HI), smem_u32(sm + P_OFF_M_LO), false, 0, 0, 0};
         const Operand tb{smem_u32(sm + P_OFF_TB_HI), smem_u32(sm + P_OFF_TB_LO), true, 8192,
                          2048, 0};
         issue_gemm(tmem + PT_P, mA, tb, ID_KM, 4);
-        mma_commit(bar_mma);
+        mma_commit_w(bar_mma);
       }
       // meanwhile: the T_b rows of [T_b; P] are the T_b tiles themselves (same swizzled
       // row image): copy hi to rows 0..63 of the hi part, lo to the lo part
