@@ -166,7 +166,7 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
 // other warps must pass a block-wide barrier afterwards.
 __device__ __forceinline__ void chunk_gates_w01(float ra, float rb, int L, float A_log,
                                                 float dtb, float* sG, float* sBeta,
-                                                int base = 0) {
+                                                int base = 0, uint32_t bar_id = 1) {
   // the two warps are threads [base, base + 64); token index t = thread - base
   const int t = threadIdx.x - base, lane = t & 31;
   const bool valid = t < L;
@@ -180,7 +180,7 @@ __device__ __forceinline__ void chunk_gates_w01(float ra, float rb, int L, float
   }
   if (t < 32) sG[t] = x;
   sBeta[t] = beta;
-  named_bar_sync(1, 64);
+  named_bar_sync(bar_id, 64);
   if (t >= 32) sG[t] = x + sG[31];
 }
 

@@ -32,7 +32,9 @@ namespace {
 using namespace sm100;
 using namespace chunk;
 
-constexpr uint32_t kA2Bytes = 24576;
+constexpr uint32_t kA2Bytes = 24576;     // [T_b; P] image: hi 16 KB | T_b lo 8 KB
+constexpr uint32_t kGateBytes = 512;     // gamma_j (64 fp32), then f_j (64 fp32)
+constexpr uint32_t kUnitBytes = kA2Bytes + kGateBytes;  // per (chunk, v-head)
 
 #ifdef GDN_PHASE_PROFILE
 // Debug-only phase timer of the scan (block 0, thread 0): clock64 deltas per phase.
@@ -223,6 +225,12 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
 
   PPHASE_INIT;
   chunk_gates(ra, rb, L, A_log, dtb, sG, sBeta);
+  if (t < kC) {  // the scan's gates: gamma_j = e^{Gamma_j}, f_j = e^{Gamma_last - Gamma_j}
+    float* gdst = reinterpret_cast<float*>(a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) *
+                                                        kUnitBytes + kA2Bytes);
+    gdst[t] = ex2(sG[t]);
+    gdst[kC + t] = (t < L) ? ex2(sG[kC - 1] - sG[t]) : 0.0f;
+  }
   PPHASE(0);  // gates
   bool ok = mbar_wait(bar_tma, 0);
   PPHASE(1);  // TMA wait
@@ -253,7 +261,7 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
       }
       // meanwhile: the T_b rows of [T_b; P] are the T_b tiles themselves (same swizzled
       // row image): copy hi to rows 0..63 of the hi part, lo to the lo part
-      uint8_t* dst = a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) * kA2Bytes;
+      uint8_t* dst = a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) * kUnitBytes;
       {
         const uint4* src_hi = reinterpret_cast<const uint4*>(sm + P_OFF_TB_HI);
         const uint4* src_lo = reinterpret_cast<const uint4*>(sm + P_OFF_TB_LO);
@@ -291,42 +299,13 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
   if (warp == 0) tmem_dealloc(tmem, kPrepTmemCols);
 }
 
-// ------------------------------------------------------------------ scan, transposed
-// One 256-thread block per (sequence, v-head): the whole 128 x 128 state. The
-// products are taken transposed so that everything the chain produces is an A
-// operand read from TMEM (lane = state row v) and every B operand is a tile that
-// arrived by TMA / bulk copy:
-//   D1 = S [K;Q]^T        -> [ (KH)^T | (QH)^T ]          (A = S hi/lo from TMEM)
-//   X^T = V^T - (KH)^T diag(gamma)                         (written to TMEM as bf16 hi/lo)
-//   D2 = X^T [T_b; P]^T   -> [ U^T | (P X)^T ]
-//   U'^T = U^T diag(f);  O^T = scale ((QH)^T diag(gamma) + (P X)^T)
-//   dS = U'^T K;  S <- gamma_last S + dS                   (S = H^T, k-last, in registers)
-// Thread t owns state row v = t % 128 and quarter c = t / 128 of every row-sliced
-// quantity (k in [32c, 32c+32) of S; j in [16c, 16c+16) of X, U; i likewise of O).
-// K/Q, V and [T_b; P] are double-buffered: chunk c+1's tiles are requested when
-// chunk c starts.
-constexpr uint32_t T_OFF_KQ = 0;          // 2 x 32 KB
-constexpr uint32_t T_OFF_A2 = 65536;      // 2 x 32 KB: hi 16 KB | lo 16 KB (rows 64..127 zero)
-constexpr uint32_t T_OFF_V = 131072;      // 2 x 16 KB: V tile, rows j x 128 v (256 B rows)
-constexpr uint32_t T_OFF_G = 163840;      // 2 x 64 fp32
-constexpr uint32_t T_OFF_BETA = 164352;   // 2 x 64 fp32 (written by the gate scan, unused)
-constexpr uint32_t T_OFF_GAM = 164864;    // 2 x 64 fp32: gamma_j = e^{Gamma_j}
-constexpr uint32_t T_OFF_F = 165376;      // 2 x 64 fp32: f_j = e^{Gamma_last - Gamma_j} (0 if padded)
-constexpr uint32_t T_OFF_BAR = 165888;    // ld[2], a2[2], mma; TMEM slot
-constexpr uint32_t T_OFF_O = 166912;      // 2 x 16 KB: output tile, rows i x 128 v (TMA store)
-constexpr uint32_t kScanTSmem = 166912 + 32768 + 1024;
+// ------------------------------------------------------------------ scan: shared pieces
 constexpr uint32_t kScanTTmemCols = 512;
-constexpr uint32_t TT_S = 0;    // S operand: hi [0, 64) | lo [64, 128); later dS (fp32, 128)
-constexpr uint32_t TT_D1 = 128; // 128 fp32 columns
-constexpr uint32_t TT_X = 256;  // X^T then U'^T operand: hi [256, 288) | lo [288, 320)
-constexpr uint32_t TT_D2 = 320; // 128 fp32 columns
 constexpr uint32_t ID_T_K = idesc_bf16(128, 128, false, false);   // B K-major
 constexpr uint32_t ID_T_MN = idesc_bf16(128, 128, false, true);   // B MN-major
 // N = 64: the lo (correction) terms are taken only for the columns that feed the state
 // (KH and U); the QH and PX columns reach the bf16 output alone and take hi x hi
 constexpr uint32_t ID_T_K64 = idesc_bf16(128, 64, false, false);
-constexpr int kScanTThreads = 512;
-constexpr int kScanTGateBase = 128;  // warps 4-5 compute the next chunk's gates
 
 struct ScanMaps {
   CUtensorMap k, q, v, o;
@@ -339,24 +318,72 @@ __device__ __forceinline__ void split_words(const float* x, uint32_t (&hi)[NW], 
   for (int w = 0; w < NW; ++w) split2(x[2 * w], x[2 * w + 1], hi[w], lo[w]);
 }
 
-__global__ void __launch_bounds__(kScanTThreads, 1)
-    scan_t_kernel(const PrefillParams p, const __grid_constant__ ScanMaps maps,
+// ------------------------------------------------------------------ scan, pipelined
+// The state product of chunk c+1 is split so that most of it leaves the chain:
+// with S_{c+1} = g_c S_c + U'_c^T K_c (g_c = gamma_last of chunk c),
+//   D1_{c+1} = S_{c+1} [K;Q]_{c+1}^T
+//            = (g_c S_c) [K;Q]_{c+1}^T          (G1a: needs only S_c)
+//            + U'_c^T ([K;Q]_{c+1} K_c^T)^T     (G1': 64-deep, after U'_c)
+// so the chain of one chunk is X_c -> G2_c -> U'_c -> G1'_c -> X_{c+1}; G1a_{c+1}, the
+// state product G3_c (dS_c = U'_c^T K_c), the state update and B_c = [K;Q]_{c+1} K_c^T
+// (exact bf16 operands) run beside it. G2_c writes its [U^T | (PX)^T] over D1_c
+// (gamma (QH)^T is parked in TMEM for the output).
+//
+// Warp roles: warps 0-15 (warpgroups 0-3, 512 threads) own the state: thread t holds
+// row v = t % 128 and quarter c = t / 128 of every row-sliced quantity (32 state
+// columns, 16 columns of X / U / output), and compute everything on CUDA cores; warp 16
+// (warpgroup 4, whose other warps idle) issues every MMA and every copy and does
+// nothing else, so that an issue that blocks on a full MMA queue never delays the
+// state warps. Registers: launched with kScanWLaunchRegs per thread; warpgroup 4 gives
+// its share down to kScanWIssuerRegs and the state warpgroups take kScanWStateRegs
+// (4 x 128 x 104 + 128 x 56 <= 640 x 96: the split must not exceed the launch total). The state warps tell the issuer that an
+// operand is ready through mbarriers (one arrival per warp); the issuer's commits
+// tell the state warps that a product is done.
+constexpr int kScanWThreads = 640;
+constexpr int kScanWState = 512;          // state threads (warps 0-15)
+constexpr uint32_t kScanWLaunchRegs = 96;
+constexpr uint32_t kScanWStateRegs = 96;
+constexpr uint32_t kScanWIssuerRegs = 96;
+static_assert(kScanWState * kScanWStateRegs + (kScanWThreads - kScanWState) * kScanWIssuerRegs <=
+                  kScanWThreads * kScanWLaunchRegs,
+              "register split exceeds the launch allocation");
+constexpr uint32_t kStateBar = 1;         // named barrier of the state threads
+constexpr uint32_t Q_OFF_KQ = 0;          // 3 x 32 KB
+constexpr uint32_t Q_OFF_A2 = 98304;      // 2 x 24 KB: [T_b; P] hi 16 KB | T_b lo 8 KB
+constexpr uint32_t Q_OFF_V = 147456;      // 2 x 16 KB: V tile, rows j x 128 v
+constexpr uint32_t Q_OFF_B = 180224;      // B_c^T image: hi 16 KB (128 rows) | lo 8 KB (K rows)
+constexpr uint32_t Q_OFF_GATES = 204800;  // 2 x (gamma_j, f_j): 2 x 512 B, from the prep
+constexpr uint32_t Q_OFF_BAR = 206848;    // 13 mbarriers, TMEM slot
+constexpr uint32_t kScanWSmem = 206848 + 256 + 1024;
+constexpr uint32_t TP_S = 0;     // operand g S: hi [0, 64) | lo [64, 128); dS (fp32) from G3
+constexpr uint32_t TP_D1 = 128;  // 2 x 128: D1 of even / odd chunks, then G2's result
+constexpr uint32_t TP_XU = 384;  // X^T, then U'^T: hi [384, 416) | lo [416, 448)
+constexpr uint32_t TP_QG = 448;  // gamma (QH)^T of the chunk, parked for the output
+// B_c^T accumulates in the first 64 columns of D1_{c+1}, free until G1a_{c+1}
+
+__global__ void __launch_bounds__(kScanWThreads, 1)
+    scan_w_kernel(const PrefillParams p, const __grid_constant__ ScanMaps maps,
                   const int64_t* __restrict__ offs, const int32_t* __restrict__ order,
                   const uint8_t* __restrict__ a2_in) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  float* sG0 = reinterpret_cast<float*>(sm + T_OFF_G);
-  float* sBeta0 = reinterpret_cast<float*>(sm + T_OFF_BETA);
-  float* sGam0 = reinterpret_cast<float*>(sm + T_OFF_GAM);
-  float* sF0 = reinterpret_cast<float*>(sm + T_OFF_F);
-  uint64_t* bar_ld = reinterpret_cast<uint64_t*>(sm + T_OFF_BAR);  // [2]
-  uint64_t* bar_a2 = bar_ld + 2;                                   // [2]
-  uint64_t* bar_mma = bar_ld + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + T_OFF_BAR + 48);
+  uint64_t* bar_kq = reinterpret_cast<uint64_t*>(sm + Q_OFF_BAR);  // [3] K/Q tiles
+  uint64_t* bar_va = bar_kq + 3;                                   // [2] V + [T_b; P]
+  uint64_t* bar_g2 = bar_kq + 5;    // commits: G2
+  uint64_t* bar_tb = bar_kq + 6;    //          B_c
+  uint64_t* bar_ch = bar_kq + 7;    //          D1 complete (G1'; G1a_0 in the prologue)
+  uint64_t* bar_g3 = bar_kq + 8;    //          G3
+  uint64_t* bar_g1a = bar_kq + 9;   //          G1a
+  uint64_t* bar_x = bar_kq + 10;    // state warps: X^T stored
+  uint64_t* bar_op = bar_kq + 11;   //              S operand and B_c image stored
+  uint64_t* bar_u = bar_kq + 12;    //              U'^T stored
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Q_OFF_BAR + 128);
 
   const int t = threadIdx.x, warp = t >> 5;
-  const int v = t & 127, ch = t >> 7;
+  const bool state_wg = t < kScanWState;
+  const bool issuer = warp == kScanWState / 32;
+  const int v = t & 127, ch = (t >> 7) & 3;
   const int h = static_cast<int>(blockIdx.x % p.HV);
   const int64_t n = order[blockIdx.x / p.HV];
   const int qh = h / (p.HV / p.HQ);
@@ -367,284 +394,395 @@ __global__ void __launch_bounds__(kScanTThreads, 1)
   // this thread's quarter of state row v: S[n, h, v, 32c .. 32c+32)
   const int64_t sbase = ((n * HV + h) * kHeadDim + v) * kHeadDim + 32 * ch;
   float S[32];
+  if (state_wg) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    const float4 x = p.state ? *reinterpret_cast<const float4*>(p.state + sbase + i)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-    S[i] = x.x; S[i + 1] = x.y; S[i + 2] = x.z; S[i + 3] = x.w;
-  }
-  if (end <= start) {  // empty sequence: pass the state through
+    for (int i = 0; i < 32; i += 4) {
+      const float4 x = p.state ? *reinterpret_cast<const float4*>(p.state + sbase + i)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      S[i] = x.x; S[i + 1] = x.y; S[i + 2] = x.z; S[i + 3] = x.w;
+    }
+    if (end <= start) {  // empty sequence: pass the state through
 #pragma unroll
-    for (int i = 0; i < 32; i += 4)
-      *reinterpret_cast<float4*>(p.new_state + sbase + i) =
-          make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
-    return;
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(p.new_state + sbase + i) =
+            make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
+    }
   }
-  const uint8_t* a2_seq = a2_in + static_cast<uint64_t>(offs[n]) * HV * kA2Bytes +
-                          static_cast<uint64_t>(h) * kA2Bytes;
-  const uint64_t a2_chunk_stride = static_cast<uint64_t>(HV) * kA2Bytes;
-
-  auto issue_loads = [&](int64_t cs, int64_t c, int b) {
-    fence_async_smem();
-    uint8_t* kq = sm + T_OFF_KQ + b * 32768;
-    mbar_arrive_expect_tx(&bar_ld[b], 4 * 8192 + 16384);
-    const int tok = static_cast<int>(cs);
-    tma_load_3d(kq, &maps.k, &bar_ld[b], 0, qh, tok);
-    tma_load_3d(kq + 8192, &maps.q, &bar_ld[b], 0, qh, tok);
-    tma_load_3d(kq + 16384, &maps.k, &bar_ld[b], 64, qh, tok);
-    tma_load_3d(kq + 16384 + 8192, &maps.q, &bar_ld[b], 64, qh, tok);
-    tma_load_3d(sm + T_OFF_V + b * 16384, &maps.v, &bar_ld[b], 0, h, tok);
-    mbar_arrive_expect_tx(&bar_a2[b], kA2Bytes);
-    const uint8_t* src = a2_seq + static_cast<uint64_t>(c) * a2_chunk_stride;
-    uint8_t* a2 = sm + T_OFF_A2 + b * 32768;
-    bulk_load(a2, src, 16384, &bar_a2[b]);
-    bulk_load(a2 + 16384, src + 16384, 8192, &bar_a2[b]);
-  };
+  if (end <= start) return;
+  const int64_t nch = (end - start + kC - 1) / kC;
 
   if (t == 0) {
-    for (int i = 0; i < 5; ++i) mbar_init(&bar_ld[i], 1);
+    for (int i = 0; i < 10; ++i) mbar_init(&bar_kq[i], 1);
+    for (int i = 10; i < 13; ++i) mbar_init(&bar_kq[i], kScanWState / 32);
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, kScanTTmemCols);
-  // rows 64..127 of the lo part of [T_b; P] stay zero (P enters as hi only)
-  for (int i = t; i < 2 * 512; i += kScanTThreads) {
-    const int b = i >> 9, q = i & 511;
-    reinterpret_cast<uint4*>(sm + T_OFF_A2 + b * 32768 + 16384 + 8192)[q] =
-        make_uint4(0u, 0u, 0u, 0u);
-  }
-  fence_async_smem();
+  if (issuer) tmem_alloc(tmem_slot, kScanTTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-
-  auto write_s_operand = [&]() {
-    uint32_t hw[16], lw[16];
-    split_words<16>(S, hw, lw);
-    tmem_st16(lane + TT_S + 16 * ch, hw);
-    tmem_st16(lane + TT_S + 64 + 16 * ch, lw);
-    tmem_st_wait();
-  };
-  write_s_operand();
-
-  const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
-  const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
-  const bool gate_thread = t >= kScanTGateBase && t < kScanTGateBase + kC;
-  auto load_gates = [&](int64_t cs, float& ra, float& rb) {
-    if (gate_thread) {
-      const int64_t tok = cs + (t - kScanTGateBase);
-      const bool valid = tok < end;
-      ra = valid ? load_scalar(p.a, p.a_dtype, tok * HV + h) : 0.0f;
-      rb = valid ? load_scalar(p.b, p.b_dtype, tok * HV + h) : 0.0f;
-    }
-  };
-  // gates of a chunk (warps 4-5): cumulative log decay, then gamma_j and f_j
-  auto gates = [&](float ra, float rb, int L, int buf) {
-    float* g = sG0 + buf * kC;
-    chunk_gates_w01(ra, rb, L, A_log, dtb, g, sBeta0 + buf * kC, kScanTGateBase);
-    named_bar_sync(1, 64);
-    const int j = t - kScanTGateBase;
-    sGam0[buf * kC + j] = ex2(g[j]);
-    sF0[buf * kC + j] = (j < L) ? ex2(g[kC - 1] - g[j]) : 0.0f;
-  };
-  float ra = 0.f, rb = 0.f;
-  load_gates(start, ra, rb);
-  if (gate_thread) gates(ra, rb, static_cast<int>((end - start) < kC ? (end - start) : kC), 0);
-  if (t == 0) issue_loads(start, 0, 0);
-
-  uint32_t mma_phase = 0;
   bool ok = true;
-  int64_t c = 0;
-#ifdef GDN_PHASE_PROFILE
-  long long sphase_last_ = clock64();
-#endif
-  for (int64_t cs = start; cs < end; cs += kC, ++c) {
-    const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
-    const int64_t next = cs + kC;
-    const int b = static_cast<int>(c & 1);
-    const uint32_t ph = static_cast<uint32_t>((c >> 1) & 1);
-    const float* sGam = sGam0 + b * kC;
-    const float* sF = sF0 + b * kC;
-    const uint8_t* kq = sm + T_OFF_KQ + b * 32768;
-    const uint8_t* a2 = sm + T_OFF_A2 + b * 32768;
-    const uint8_t* vt = sm + T_OFF_V + b * 16384;
-    float nra = 0.f, nrb = 0.f;
-    if (next < end) load_gates(next, nra, nrb);
 
-    SPHASE(0);  // top: next loads issued
-    // ---- D1 = S [K;Q]^T ---------------------------------------------------------------
-    ok = mbar_wait(&bar_ld[b], ph);
-    SPHASE(1);  // K/Q/V wait
-    tc_fence_before();
-    if (!__syncthreads_and(ok)) break;  // also: the S operand of every thread is stored
-    tc_fence_after();
-    SPHASE(10);  // top barrier
-    if (warp == 0) {
-      __syncwarp();
+  if constexpr (kScanWStateRegs != kScanWLaunchRegs) {
+    if (!state_wg) {
+      setmaxnreg_dec<kScanWIssuerRegs>();
+    } else {
+      setmaxnreg_inc<kScanWStateRegs>();
+    }
+  }
+  if (issuer) {
+    // ================================ MMA / copy issuer ================================
+    const uint8_t* a2_seq = a2_in + static_cast<uint64_t>(offs[n]) * HV * kUnitBytes +
+                            static_cast<uint64_t>(h) * kUnitBytes;
+    const uint64_t a2_chunk_stride = static_cast<uint64_t>(HV) * kUnitBytes;
+    const bool leader = (t & 31) == 0;
+    auto issue_kq = [&](int64_t m) {  // chunk m's K/Q tile -> buffer m % 3
+      const int bq = static_cast<int>(m % 3);
+      uint8_t* kq = sm + Q_OFF_KQ + bq * 32768;
+      mbar_arrive_expect_tx(&bar_kq[bq], 4 * 8192);
+      const int tok = static_cast<int>(start + m * kC);
+      tma_load_3d(kq, &maps.k, &bar_kq[bq], 0, qh, tok);
+      tma_load_3d(kq + 8192, &maps.q, &bar_kq[bq], 0, qh, tok);
+      tma_load_3d(kq + 16384, &maps.k, &bar_kq[bq], 64, qh, tok);
+      tma_load_3d(kq + 16384 + 8192, &maps.q, &bar_kq[bq], 64, qh, tok);
+    };
+    // chunk m's V tile, [T_b; P] image and gates -> buffer m & 1
+    auto issue_va = [&](int64_t m) {
+      const int b = static_cast<int>(m & 1);
+      mbar_arrive_expect_tx(&bar_va[b], 16384 + kUnitBytes);
+      tma_load_3d(sm + Q_OFF_V + b * 16384, &maps.v, &bar_va[b], 0, h,
+                  static_cast<int>(start + m * kC));
+      const uint8_t* src = a2_seq + static_cast<uint64_t>(m) * a2_chunk_stride;
+      uint8_t* a2 = sm + Q_OFF_A2 + b * kA2Bytes;
+      bulk_load(a2, src, 16384, &bar_va[b]);
+      bulk_load(a2 + 16384, src + 16384, 8192, &bar_va[b]);
+      bulk_load(sm + Q_OFF_GATES + b * kGateBytes, src + kA2Bytes, kGateBytes, &bar_va[b]);
+    };
+    // G1a: D1 (columns d) = (operand columns) [K;Q]^T of the tile kq
+    auto issue_g1a = [&](uint32_t d, const uint8_t* kq) {
       const uint64_t bd = desc_kmajor(smem_u32(kq));
 #pragma unroll
       for (int s = 0; s < 8; ++s)
-        mma_bf16_ts_w(tmem + TT_D1, tmem + TT_S + s * 8,
-                    bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, s > 0);
+        mma_bf16_ts_w(tmem + d, tmem + TP_S + s * 8,
+                      bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, s > 0);
 #pragma unroll
       for (int s = 0; s < 8; ++s)
-        mma_bf16_ts_w(tmem + TT_D1, tmem + TT_S + 64 + s * 8,
-                    bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K64, 1);
-      mma_commit_w(bar_mma);
-    }
-    // chunk c+1's tiles into the other buffers (their last users, chunk c-1, are done),
-    // from another warp while thread 0 is blocked issuing the MMAs
-    if (t == 32 && next < end) issue_loads(next, c + 1, b ^ 1);
-    if (gate_thread && next < end)
-      gates(nra, nrb, static_cast<int>((end - next) < kC ? (end - next) : kC), b ^ 1);
-    SPHASE(2);  // sync + G1 issue + gates
-    ok = mbar_wait(bar_mma, mma_phase);
-    mma_phase ^= 1;
-    tc_fence_after();
-    if (!__syncthreads_and(ok)) break;
-    SPHASE(3);  // G1 wait
-
-    {
-      // X^T row v, columns j in [16c, 16c+16): V[j][v] - gamma_j (KH)^T[v][j]
-      float d[16];
-      tmem_ld16(lane + TT_D1 + 16 * ch, d);
-      tmem_ld_wait();
-      float x[16];
+        mma_bf16_ts_w(tmem + d, tmem + TP_S + 64 + s * 8,
+                      bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K64, 1);
+    };
+    // B_m^T = [K;Q]_{m+1} K_m^T (exact bf16 operands, one term) into the first 64
+    // columns of D1_{m+1}'s buffer (free until G1a_{m+1})
+    auto issue_b = [&](int64_t m) -> bool {
+      const bool w = mbar_wait(&bar_kq[(m + 1) % 3], static_cast<uint32_t>(((m + 1) / 3) & 1));
+      tc_fence_after();
+      __syncwarp();
+      if (!w) return false;
+      const uint8_t* kqm = sm + Q_OFF_KQ + static_cast<int>(m % 3) * 32768;
+      const uint8_t* kqm1 = sm + Q_OFF_KQ + static_cast<int>((m + 1) % 3) * 32768;
+      const uint64_t an = desc_kmajor(smem_u32(kqm1)), bc = desc_kmajor(smem_u32(kqm));
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int j = 16 * ch + i;
-        const unsigned short raw =
-            *reinterpret_cast<const unsigned short*>(vt + j * 256 + v * 2);
-        x[i] = __uint_as_float(static_cast<uint32_t>(raw) << 16) - sGam[j] * d[i];
+      for (int s = 0; s < 8; ++s) {
+        const uint64_t off = ((s >> 2) * 16384 + (s & 3) * 32) >> 4;
+        mma_bf16_w(tmem + TP_D1 + 128 * static_cast<uint32_t>((m + 1) & 1), an + off, bc + off,
+                   ID_KK, s > 0);
       }
-      uint32_t hw[8], lw[8];
-      split_words<8>(x, hw, lw);
-      tmem_st8(lane + TT_X + 8 * ch, hw);
-      tmem_st8(lane + TT_X + 32 + 8 * ch, lw);
-      tmem_st_wait();
+      mma_commit_w(bar_tb);
+      return true;
+    };
+    if (leader) {
+      issue_kq(0);
+      issue_va(0);
+      if (nch > 1) {
+        issue_kq(1);
+        issue_va(1);
+      }
     }
+    __syncwarp();
+    uint32_t ph_x = 0, ph_op = 0, ph_u = 0, ph_g2 = 0, ph_g3 = 0, ph_g1a = 0;
+    // prologue: D1_0 = S_0 [K;Q]_0^T
+    ok = mbar_wait(bar_op, ph_op) && ok;
+    ph_op ^= 1;
+    ok = mbar_wait(&bar_kq[0], 0) && ok;
+    tc_fence_after();
+    __syncwarp();
+    if (ok) {
+      issue_g1a(TP_D1, sm + Q_OFF_KQ);
+      mma_commit_w(bar_ch);
+      if (nch > 1) ok = issue_b(0);
+    }
+    for (int64_t c = 0; ok && c < nch; ++c) {
+      const bool last = c == nch - 1;
+      const int b = static_cast<int>(c & 1);
+      const uint32_t d1c = TP_D1 + 128 * b, d1n = TP_D1 + 128 * (b ^ 1);
+      const uint8_t* kqc = sm + Q_OFF_KQ + static_cast<int>(c % 3) * 32768;
+      const uint8_t* kqn = sm + Q_OFF_KQ + static_cast<int>((c + 1) % 3) * 32768;
+      const uint8_t* a2 = sm + Q_OFF_A2 + b * kA2Bytes;
+      if (c > 0) {
+        // G2_{c-1} and G3_{c-1} done: chunk c-1's K/Q, V and [T_b; P] buffers are free
+        ok = mbar_wait(bar_g2, ph_g2) && ok;
+        ph_g2 ^= 1;
+        ok = mbar_wait(bar_g3, ph_g3) && ok;
+        ph_g3 ^= 1;
+        if (!ok) break;
+      }
+      // chunk c+2's K/Q tile (third buffer; chunk c-1's for c > 0) and chunk c+1's V and
+      // [T_b; P] (chunk c-1's buffers; chunk 1's were requested with chunk 0's)
+      if (leader) {
+        if (c + 2 < nch) issue_kq(c + 2);
+        if (c > 0 && c + 1 < nch) issue_va(c + 1);
+      }
+      __syncwarp();
+      // ---- G2_c: D1_c <- X^T [T_b; P]^T = [U^T | (PX)^T] ----------------------------
+      ok = mbar_wait(bar_x, ph_x) && ok;
+      ph_x ^= 1;
+      ok = mbar_wait(&bar_va[b], static_cast<uint32_t>((c >> 1) & 1)) && ok;
+      tc_fence_after();
+      __syncwarp();
+      if (!ok) break;
+      {
+        const uint64_t bh = desc_kmajor(smem_u32(a2)), bl = desc_kmajor(smem_u32(a2 + 16384));
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16_ts_w(tmem + d1c, tmem + TP_XU + s * 8, bh + ((s * 32) >> 4), ID_T_K, s > 0);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16_ts_w(tmem + d1c, tmem + TP_XU + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K64,
+                        1);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16_ts_w(tmem + d1c, tmem + TP_XU + s * 8, bl + ((s * 32) >> 4), ID_T_K64, 1);
+        mma_commit_w(bar_g2);
+      }
+      if (!last) {
+        // ---- G1a_{c+1} = (g_c S_c) [K;Q]_{c+1}^T once the operand is stored -------------
+        ok = mbar_wait(bar_op, ph_op) && ok;
+        ph_op ^= 1;
+        tc_fence_after();
+        __syncwarp();
+        if (!ok) break;
+        issue_g1a(d1n, kqn);
+        mma_commit_w(bar_g1a);
+      }
+      // ---- U'_c stored: G1'_c onto D1_{c+1}, then G3_c: dS_c = U'^T K_c ----------------
+      ok = mbar_wait(bar_u, ph_u) && ok;
+      ph_u ^= 1;
+      tc_fence_after();
+      __syncwarp();
+      if (!ok) break;
+      if (!last) {
+        const uint64_t bh = desc_kmajor(smem_u32(sm + Q_OFF_B));
+        const uint64_t bl = desc_kmajor(smem_u32(sm + Q_OFF_B + 16384));
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16_ts_w(tmem + d1n, tmem + TP_XU + s * 8, bh + ((s * 32) >> 4), ID_T_K, 1);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16_ts_w(tmem + d1n, tmem + TP_XU + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K64,
+                        1);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16_ts_w(tmem + d1n, tmem + TP_XU + s * 8, bl + ((s * 32) >> 4), ID_T_K64, 1);
+        mma_commit_w(bar_ch);
+        // G3 overwrites the operand columns that G1a_{c+1} reads (another accumulator:
+        // no implicit order between them)
+        ok = mbar_wait(bar_g1a, ph_g1a) && ok;
+        ph_g1a ^= 1;
+        tc_fence_after();
+        __syncwarp();
+        if (!ok) break;
+      }
+      {
+        const uint64_t bk = desc_mnmajor(smem_u32(kqc), 16384);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16_ts_w(tmem + TP_S, tmem + TP_XU + s * 8, bk + ((s * 2048) >> 4), ID_T_MN,
+                        s > 0);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          mma_bf16_ts_w(tmem + TP_S, tmem + TP_XU + 32 + s * 8, bk + ((s * 2048) >> 4), ID_T_MN,
+                        1);
+        mma_commit_w(bar_g3);
+      }
+      // B_{c+1} for chunk c+1's state-side work (D1_c's buffer is read: U'_c is stored)
+      if (c + 2 < nch && !issue_b(c + 1)) {
+        ok = false;
+        break;
+      }
+    }
+  } else if (state_wg) {
+    // ================================ state warps ======================================
+    const uint32_t lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const bool lane0 = (t & 31) == 0;
+    // this warp's arrival on a ready barrier: every lane's TMEM stores have completed
+    // and its shared-memory writes are visible to the tensor core
+    auto signal = [&](uint64_t* bar) {
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane0) mbar_arrive(bar);
+    };
+    // the S operand: bf16 hi/lo of scale * S (this thread's 32 columns)
+    auto write_s_operand = [&](float scale) {
+      uint32_t hw[16], lw[16];
+#pragma unroll
+      for (int w = 0; w < 16; ++w) split2(scale * S[2 * w], scale * S[2 * w + 1], hw[w], lw[w]);
+      tmem_st16(lane + TP_S + 16 * ch, hw);
+      tmem_st16(lane + TP_S + 64 + 16 * ch, lw);
+      tmem_st_wait();
+    };
+    // prologue: the operand S_0 for D1_0
+    write_s_operand(1.0f);
+    signal(bar_op);
 
-    SPHASE(4);  // X build
-    // ---- D2 = X^T [T_b; P]^T -----------------------------------------------------------
-    ok = mbar_wait(&bar_a2[b], ph);
-    tc_fence_before();
-    if (!__syncthreads_and(ok)) break;
-    tc_fence_after();
-    if (warp == 0) {
-      __syncwarp();
-      const uint64_t bh = desc_kmajor(smem_u32(a2)), bl = desc_kmajor(smem_u32(a2 + 16384));
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        mma_bf16_ts_w(tmem + TT_D2, tmem + TT_X + s * 8, bh + ((s * 32) >> 4), ID_T_K, s > 0);
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        mma_bf16_ts_w(tmem + TT_D2, tmem + TT_X + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K64, 1);
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        mma_bf16_ts_w(tmem + TT_D2, tmem + TT_X + s * 8, bl + ((s * 32) >> 4), ID_T_K64, 1);
-      mma_commit_w(bar_mma);
-    }
-    SPHASE(5);  // A2 wait + sync + G2 issue
-    ok = mbar_wait(bar_mma, mma_phase);
-    mma_phase ^= 1;
-    tc_fence_after();
-    if (!__syncthreads_and(ok)) break;
-    SPHASE(6);  // G2 wait
-    {
-      // U'^T = U^T diag(f) -> operand (over X^T, consumed)
-      float u[16];
-      tmem_ld16(lane + TT_D2 + 16 * ch, u);
-      tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 16; ++i) u[i] *= sF[16 * ch + i];
-      uint32_t hw[8], lw[8];
-      split_words<8>(u, hw, lw);
-      tmem_st8(lane + TT_X + 8 * ch, hw);
-      tmem_st8(lane + TT_X + 32 + 8 * ch, lw);
-      tmem_st_wait();
-    }
-    SPHASE(7);  // U' + O
-    // ---- dS = U'^T K (into the S operand columns: G1 is done) ---------------------------
-    if (t == 0) bulk_wait_read<1>();  // this chunk's output tile buffer is free again
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 0) {
-      __syncwarp();
-      const uint64_t bk = desc_mnmajor(smem_u32(kq), 16384);
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        mma_bf16_ts_w(tmem + TT_S, tmem + TT_X + s * 8, bk + ((s * 2048) >> 4), ID_T_MN, s > 0);
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        mma_bf16_ts_w(tmem + TT_S, tmem + TT_X + 32 + s * 8, bk + ((s * 2048) >> 4), ID_T_MN, 1);
-      mma_commit_w(bar_mma);
-    }
-    {
-      // while dS is computed: O^T row v, tokens i in [32c, 32c+32) (D1 and D2 columns
-      // that the state-update MMA does not touch)
-      float o[16], qv[16];
-      tmem_ld16(lane + TT_D2 + 64 + 16 * ch, o);
-      tmem_ld16(lane + TT_D1 + 64 + 16 * ch, qv);
-      tmem_ld_wait();
-      if (L == kC) {
-        // full chunk: stage the tile, one TMA store after the next barrier
-        __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(sm + T_OFF_O + b * 16384);
+    uint32_t ph_ch = 0, ph_g2 = 0, ph_tb = 0, ph_g3 = 0;
+    float g_prev = 1.0f;  // gamma_last of the previous chunk
+#ifdef GDN_PHASE_PROFILE
+    long long sphase_last_ = clock64();
+#endif
+    for (int64_t c = 0; c < nch; ++c) {
+      const int64_t cs = start + c * kC;
+      const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
+      const bool last = c == nch - 1;
+      const int b = static_cast<int>(c & 1);
+      const uint32_t d1c = TP_D1 + 128 * b, d1n = TP_D1 + 128 * (b ^ 1);
+      // gates of chunk c (from the prep, arrived with the [T_b; P] image)
+      const float* sGam = reinterpret_cast<const float*>(sm + Q_OFF_GATES + b * kGateBytes);
+      const float* sF = sGam + kC;
+      const uint8_t* vt = sm + Q_OFF_V + b * 16384;
+      SPHASE(0);
+      // ---- D1_c complete: X_c^T = V^T - (KH)^T diag(gamma); keep gamma (QH)^T --------
+      ok = mbar_wait(bar_ch, ph_ch) && ok;
+      ph_ch ^= 1;
+      ok = mbar_wait(&bar_va[b], static_cast<uint32_t>((c >> 1) & 1)) && ok;
+      tc_fence_after();
+      SPHASE(1);  // D1 wait
+      {
+        float d[16], qg[16];
+        tmem_ld16(lane + d1c + 16 * ch, d);
+        tmem_ld16(lane + d1c + 64 + 16 * ch, qg);
+        tmem_ld_wait();
+        float x[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int ii = 16 * ch + i;
-          tile[ii * kHeadDim + v] = __float2bfloat16_rn(p.scale * fmaf(sGam[ii], qv[i], o[i]));
+          const int j = 16 * ch + i;
+          const float gj = sGam[j];
+          const unsigned short raw =
+              *reinterpret_cast<const unsigned short*>(vt + j * 256 + v * 2);
+          x[i] = __uint_as_float(static_cast<uint32_t>(raw) << 16) - gj * d[i];
+          qg[i] *= gj;
         }
-      } else {
-        // partial (last) chunk: only its own tokens; rows past L belong to the next sequence
+        uint32_t hw[8], lw[8];
+        split_words<8>(x, hw, lw);
+        if (c > 0) {  // G3_{c-1} has read U'_{c-1} and written dS_{c-1}
+          ok = mbar_wait(bar_g3, ph_g3) && ok;
+          ph_g3 ^= 1;
+          tc_fence_after();
+        }
+        tmem_st8(lane + TP_XU + 8 * ch, hw);
+        tmem_st8(lane + TP_XU + 32 + 8 * ch, lw);
+        uint32_t qw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) qw[i] = __float_as_uint(qg[i]);
+        tmem_st16(lane + TP_QG + 16 * ch, qw);
+        tmem_st_wait();
+      }
+      signal(bar_x);
+      SPHASE(2);  // X build
+
+      // ---- beside the chain: S_c = g_{c-1} S_{c-1} + dS_{c-1}; operand g_c S_c; B_c ------
+      if (c > 0) {
+        float d0[32];
+        tmem_ld32(lane + TP_S + 32 * ch, d0);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) S[i] = fmaf(g_prev, S[i], d0[i]);
+      }
+      g_prev = sGam[kC - 1];
+      if (!last) {
+        tc_fence_before();
+        // every state thread has read dS_{c-1}
+        if (!named_bar_and(kStateBar, kScanWState, ok)) break;
+        tc_fence_after();
+        write_s_operand(g_prev);
+        ok = mbar_wait(bar_tb, ph_tb) && ok;
+        ph_tb ^= 1;
+        tc_fence_after();
+        {
+          // row v of B_c^T (the [K;Q]_{c+1} row), columns i in [16c, 16c+16)
+          float bt[16];
+          tmem_ld16(lane + d1n + 16 * ch, bt);
+          tmem_ld_wait();
+          uint32_t hw[8], lw[8];
+          split_words<8>(bt, hw, lw);
+          uint8_t* bimg = sm + Q_OFF_B;
+          *reinterpret_cast<uint4*>(bimg + sw128_chunk(v, 2 * ch)) =
+              make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(bimg + sw128_chunk(v, 2 * ch + 1)) =
+              make_uint4(hw[4], hw[5], hw[6], hw[7]);
+          if (v < kC) {  // lo for the K rows only (the Q rows reach the output alone)
+            *reinterpret_cast<uint4*>(bimg + 16384 + sw128_chunk(v, 2 * ch)) =
+                make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            *reinterpret_cast<uint4*>(bimg + 16384 + sw128_chunk(v, 2 * ch + 1)) =
+                make_uint4(lw[4], lw[5], lw[6], lw[7]);
+          }
+        }
+        signal(bar_op);
+      }
+      SPHASE(3);  // state update, operand, B image
+
+      // ---- G2_c done: U'^T = U^T diag(f) (over X^T); output rows of chunk c -------------
+      ok = mbar_wait(bar_g2, ph_g2) && ok;
+      ph_g2 ^= 1;
+      tc_fence_after();
+      SPHASE(4);  // G2 wait
+      {
+        float u[16], o[16];
+        tmem_ld16(lane + d1c + 16 * ch, u);
+        tmem_ld16(lane + d1c + 64 + 16 * ch, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) u[i] *= sF[16 * ch + i];
+        uint32_t hw[8], lw[8];
+        split_words<8>(u, hw, lw);
+        tmem_st8(lane + TP_XU + 8 * ch, hw);
+        tmem_st8(lane + TP_XU + 32 + 8 * ch, lw);
+        tmem_st_wait();
+        signal(bar_u);
+        float qg[16];
+        tmem_ld16(lane + TP_QG + 16 * ch, qg);
+        tmem_ld_wait();
         __nv_bfloat16* dst = p.out + (cs * HV + h) * kHeadDim + v;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int ii = 16 * ch + i;
           if (ii < L)
             dst[static_cast<int64_t>(ii) * HV * kHeadDim] =
-                __float2bfloat16_rn(p.scale * fmaf(sGam[ii], qv[i], o[i]));
+                __float2bfloat16_rn(p.scale * (qg[i] + o[i]));
         }
       }
-      fence_async_smem();
+      SPHASE(5);  // U' and output
     }
-    ok = mbar_wait(bar_mma, mma_phase);
-    mma_phase ^= 1;
-    tc_fence_after();
-    if (!__syncthreads_and(ok)) break;
-    SPHASE(8);  // sync + G3 issue + O + wait
-    {
+    if (ok) {
+      ok = mbar_wait(bar_g3, ph_g3);
+      tc_fence_after();
+    }
+    if (named_bar_and(kStateBar, kScanWState, ok)) {
       float d0[32];
-      tmem_ld32(lane + TT_S + 32 * ch, d0);
+      tmem_ld32(lane + TP_S + 32 * ch, d0);
       tmem_ld_wait();
-      const float gl = sGam[kC - 1];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) S[i] = fmaf(gl, S[i], d0[i]);
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(p.new_state + sbase + i) =
+            make_float4(fmaf(g_prev, S[i], d0[i]), fmaf(g_prev, S[i + 1], d0[i + 1]),
+                        fmaf(g_prev, S[i + 2], d0[i + 2]), fmaf(g_prev, S[i + 3], d0[i + 3]));
+    } else {
+      ok = false;
     }
-    tc_fence_before();
-    __syncthreads();  // every thread has read its dS columns before they are overwritten
-    tc_fence_after();
-    if (t == 0 && L == kC) {
-      tma_store_3d(&maps.o, sm + T_OFF_O + b * 16384, 0, h, static_cast<int>(cs));
-      bulk_commit();
-    }
-    write_s_operand();
-    SPHASE(9);  // S update + operand
   }
-
-  if (t == 0) bulk_wait_all();  // output stores complete before the block exits
-  if (ok) {
-#pragma unroll
-    for (int i = 0; i < 32; i += 4)
-      *reinterpret_cast<float4*>(p.new_state + sbase + i) =
-          make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
-  } else if (t == 0 && p.status) {
-    atomicExch(p.status, 1);
-  }
+  if (!ok && p.status) atomicExch(p.status, 1);
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, kScanTTmemCols);
+  if (issuer) tmem_dealloc(tmem, kScanTTmemCols);
 }
 
 bool encode_v_map(CUtensorMap* map, const void* base, int64_t T, int HV) {
@@ -674,7 +812,7 @@ static size_t head_bytes(int64_t N) {
 size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV) {
   const size_t head = head_bytes(N);
   const size_t chunks = static_cast<size_t>((T + kC - 1) / kC + N);
-  return head + chunks * static_cast<size_t>(HV) * kA2Bytes;
+  return head + chunks * static_cast<size_t>(HV) * kUnitBytes;
 }
 
 int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_t stream) {
@@ -705,10 +843,21 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   const void* vb = p.T > 0 ? static_cast<const void*>(p.v) : static_cast<const void*>(p.new_state);
   void* ob = p.T > 0 ? static_cast<void*>(p.out) : static_cast<void*>(p.new_state);
   if (!encode_v_map(&smaps.v, vb, Tm, p.HV) || !encode_v_map(&smaps.o, ob, Tm, p.HV)) return -2;
-  if (cudaFuncSetAttribute(scan_t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kScanTSmem) != cudaSuccess)
+  if (cudaFuncSetAttribute(scan_w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kScanWSmem) != cudaSuccess)
     return -1;
-  scan_t_kernel<<<static_cast<unsigned>(p.N * p.HV), kScanTThreads, kScanTSmem, stream>>>(
+  // The warpgroups' register split (setmaxnreg) must fit in what the block is launched
+  // with; a build whose launch register count came out lower is not run.
+  static int launch_regs = -1;
+  if (launch_regs < 0) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, scan_w_kernel) != cudaSuccess) return -1;
+    launch_regs = fa.numRegs;
+  }
+  if (static_cast<uint32_t>(launch_regs) * kScanWThreads <
+      kScanWState * kScanWStateRegs + (kScanWThreads - kScanWState) * kScanWIssuerRegs)
+    return -1;
+  scan_w_kernel<<<static_cast<unsigned>(p.N * p.HV), kScanWThreads, kScanWSmem, stream>>>(
       p, smaps, offs, order, a2);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
