@@ -39,13 +39,31 @@ constexpr uint32_t kUnitBytes = kA2Bytes + kGateBytes;  // per (chunk, v-head)
 #ifdef GDN_PHASE_PROFILE
 // Debug-only phase timer of the scan (block 0, thread 0): clock64 deltas per phase.
 __device__ long long g_scan_cycles[16];
+// (accumulated in shared memory, `sprof_`, and added to g_scan_cycles at exit)
 #define SPHASE(i)                                     \
   do {                                                \
     if (blockIdx.x == 0 && threadIdx.x == 0) {        \
       const long long now_ = clock64();               \
-      g_scan_cycles[i] += now_ - sphase_last_;        \
+      sprof_[i] += now_ - sphase_last_;               \
       sphase_last_ = now_;                            \
     }                                                 \
+  } while (0)
+#define IPHASE(i)                                     \
+  do {                                                \
+    if (blockIdx.x == 0 && threadIdx.x == 512) {      \
+      const long long now_ = clock64();               \
+      sprof_[8 + (i)] += now_ - iphase_last_;         \
+      iphase_last_ = now_;                            \
+    }                                                 \
+  } while (0)
+// Debug event timestamps of one chunk (block 0, chunk kEventChunk), state thread 0 and
+// the issuer: clock64 values, SM-local.
+__device__ long long g_scan_events[32];
+constexpr int64_t kEventChunk = 100;
+#define SEVENT(i)                                                             \
+  do {                                                                        \
+    if (blockIdx.x == 0 && c == kEventChunk && (threadIdx.x == 0 || threadIdx.x == 512)) \
+      g_scan_events[i] = clock64();                                           \
   } while (0)
 __device__ long long g_prep_cycles[16];
 #define PPHASE(i)                                     \
@@ -65,6 +83,12 @@ __device__ long long g_prep_cycles[16];
   do {            \
   } while (0)
 #define PPHASE_INIT
+#define IPHASE(i) \
+  do {            \
+  } while (0)
+#define SEVENT(i) \
+  do {            \
+  } while (0)
 #endif  // per (chunk, v-head): hi 16 KB + lo rows 0..63 8 KB
 
 __device__ __forceinline__ void seq_bounds(const PrefillParams& p, int64_t n, int64_t& start,
@@ -354,12 +378,18 @@ constexpr uint32_t Q_OFF_V = 147456;      // 2 x 16 KB: V tile, rows j x 128 v
 constexpr uint32_t Q_OFF_B = 180224;      // B_c^T image: hi 16 KB (128 rows) | lo 8 KB (K rows)
 constexpr uint32_t Q_OFF_GATES = 204800;  // 2 x (gamma_j, f_j): 2 x 512 B, from the prep
 constexpr uint32_t Q_OFF_BAR = 206848;    // 13 mbarriers, TMEM slot
-constexpr uint32_t kScanWSmem = 206848 + 256 + 1024;
-constexpr uint32_t TP_S = 0;     // operand g S: hi [0, 64) | lo [64, 128); dS (fp32) from G3
-constexpr uint32_t TP_D1 = 128;  // 2 x 128: D1 of even / odd chunks, then G2's result
-constexpr uint32_t TP_XU = 384;  // X^T, then U'^T: hi [384, 416) | lo [416, 448)
-constexpr uint32_t TP_QG = 448;  // gamma (QH)^T of the chunk, parked for the output
-// B_c^T accumulates in the first 64 columns of D1_{c+1}, free until G1a_{c+1}
+constexpr uint32_t Q_OFF_PROF = 206848 + 256;  // debug phase timers (16 x 8 B)
+constexpr uint32_t kScanWSmem = 206848 + 512 + 1024;
+// operand g S: thread quarter c writes columns [32c, 32c + 32) as 16 hi words then 16 lo
+// words (K step s: hi at 32 (s/2) + 8 (s%2), lo 16 further); dS (fp32) from G3
+constexpr uint32_t TP_S = 0;
+// D1 of even / odd chunks: [(KH)^T | (QH)^T]. Each thread then writes X^T, later U'^T,
+// over its own 16 fp32 columns of (KH)^T as 8 hi words followed by 8 lo words (so no
+// thread overwrites columns another thread has yet to read); as an A operand, K step s
+// is hi at column 16 s and lo at 16 s + 8. B_{c}^T accumulates in the (QH)^T half of
+// D1_{c+1}'s buffer, free until G1a_{c+1}.
+constexpr uint32_t TP_D1 = 128;  // 2 x 128
+constexpr uint32_t TP_GO = 384;  // G2's result [U^T | (PX)^T]
 
 __global__ void __launch_bounds__(kScanWThreads, 1)
     scan_w_kernel(const PrefillParams p, const __grid_constant__ ScanMaps maps,
@@ -379,6 +409,10 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   uint64_t* bar_op = bar_kq + 11;   //              S operand and B_c image stored
   uint64_t* bar_u = bar_kq + 12;    //              U'^T stored
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Q_OFF_BAR + 128);
+#ifdef GDN_PHASE_PROFILE
+  long long* sprof_ = reinterpret_cast<long long*>(sm + Q_OFF_PROF);
+  if (threadIdx.x < 16) sprof_[threadIdx.x] = 0;
+#endif
 
   const int t = threadIdx.x, warp = t >> 5;
   const bool state_wg = t < kScanWState;
@@ -463,17 +497,17 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       const uint64_t bd = desc_kmajor(smem_u32(kq));
 #pragma unroll
       for (int s = 0; s < 8; ++s)
-        mma_bf16_ts_w(tmem + d, tmem + TP_S + s * 8,
+        mma_bf16_ts_w(tmem + d, tmem + TP_S + 32 * (s >> 1) + 8 * (s & 1),
                       bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, s > 0);
 #pragma unroll
       for (int s = 0; s < 8; ++s)
-        mma_bf16_ts_w(tmem + d, tmem + TP_S + 64 + s * 8,
+        mma_bf16_ts_w(tmem + d, tmem + TP_S + 32 * (s >> 1) + 16 + 8 * (s & 1),
                       bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K64, 1);
     };
     // B_m^T = [K;Q]_{m+1} K_m^T (exact bf16 operands, one term) into the first 64
     // columns of D1_{m+1}'s buffer (free until G1a_{m+1})
     auto issue_b = [&](int64_t m) -> bool {
-      const bool w = mbar_wait(&bar_kq[(m + 1) % 3], static_cast<uint32_t>(((m + 1) / 3) & 1));
+      const bool w = mbar_wait_spin(&bar_kq[(m + 1) % 3], static_cast<uint32_t>(((m + 1) / 3) & 1));
       tc_fence_after();
       __syncwarp();
       if (!w) return false;
@@ -483,8 +517,8 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         const uint64_t off = ((s >> 2) * 16384 + (s & 3) * 32) >> 4;
-        mma_bf16_w(tmem + TP_D1 + 128 * static_cast<uint32_t>((m + 1) & 1), an + off, bc + off,
-                   ID_KK, s > 0);
+        mma_bf16_w(tmem + TP_D1 + 128 * static_cast<uint32_t>((m + 1) & 1) + 64, an + off,
+                   bc + off, ID_KK, s > 0);
       }
       mma_commit_w(bar_tb);
       return true;
@@ -498,11 +532,11 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       }
     }
     __syncwarp();
-    uint32_t ph_x = 0, ph_op = 0, ph_u = 0, ph_g2 = 0, ph_g3 = 0, ph_g1a = 0;
+    uint32_t ph_x = 0, ph_op = 0, ph_u = 0, ph_g1a = 0;
     // prologue: D1_0 = S_0 [K;Q]_0^T
-    ok = mbar_wait(bar_op, ph_op) && ok;
+    ok = mbar_wait_spin(bar_op, ph_op) && ok;
     ph_op ^= 1;
-    ok = mbar_wait(&bar_kq[0], 0) && ok;
+    ok = mbar_wait_spin(&bar_kq[0], 0) && ok;
     tc_fence_after();
     __syncwarp();
     if (ok) {
@@ -510,6 +544,9 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       mma_commit_w(bar_ch);
       if (nch > 1) ok = issue_b(0);
     }
+#ifdef GDN_PHASE_PROFILE
+    long long iphase_last_ = clock64();
+#endif
     for (int64_t c = 0; ok && c < nch; ++c) {
       const bool last = c == nch - 1;
       const int b = static_cast<int>(c & 1);
@@ -517,54 +554,60 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       const uint8_t* kqc = sm + Q_OFF_KQ + static_cast<int>(c % 3) * 32768;
       const uint8_t* kqn = sm + Q_OFF_KQ + static_cast<int>((c + 1) % 3) * 32768;
       const uint8_t* a2 = sm + Q_OFF_A2 + b * kA2Bytes;
-      if (c > 0) {
-        // G2_{c-1} and G3_{c-1} done: chunk c-1's K/Q, V and [T_b; P] buffers are free
-        ok = mbar_wait(bar_g2, ph_g2) && ok;
-        ph_g2 ^= 1;
-        ok = mbar_wait(bar_g3, ph_g3) && ok;
-        ph_g3 ^= 1;
-        if (!ok) break;
-      }
-      // chunk c+2's K/Q tile (third buffer; chunk c-1's for c > 0) and chunk c+1's V and
-      // [T_b; P] (chunk c-1's buffers; chunk 1's were requested with chunk 0's)
-      if (leader) {
-        if (c + 2 < nch) issue_kq(c + 2);
-        if (c > 0 && c + 1 < nch) issue_va(c + 1);
-      }
+      // chunk c+1's V, [T_b; P] and gates into chunk c-1's buffers (chunk 1's were
+      // requested with chunk 0's): their readers, X_{c-1} and G2_{c-1}, finished before
+      // U'_{c-1} was signalled
+      if (leader && c > 0 && c + 1 < nch) issue_va(c + 1);
       __syncwarp();
+      IPHASE(0);  // loads
+      SEVENT(16);
       // ---- G2_c: D1_c <- X^T [T_b; P]^T = [U^T | (PX)^T] ----------------------------
-      ok = mbar_wait(bar_x, ph_x) && ok;
+      ok = mbar_wait_spin(bar_x, ph_x) && ok;
       ph_x ^= 1;
-      ok = mbar_wait(&bar_va[b], static_cast<uint32_t>((c >> 1) & 1)) && ok;
+      SEVENT(24);
+      ok = mbar_wait_spin(&bar_va[b], static_cast<uint32_t>((c >> 1) & 1)) && ok;
       tc_fence_after();
       __syncwarp();
       if (!ok) break;
+      IPHASE(1);  // X wait
+      SEVENT(17);
       {
         const uint64_t bh = desc_kmajor(smem_u32(a2)), bl = desc_kmajor(smem_u32(a2 + 16384));
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1c, tmem + TP_XU + s * 8, bh + ((s * 32) >> 4), ID_T_K, s > 0);
+          mma_bf16_ts_w(tmem + TP_GO, tmem + d1c + 16 * s, bh + ((s * 32) >> 4), ID_T_K, s > 0);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1c, tmem + TP_XU + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K64,
-                        1);
+          mma_bf16_ts_w(tmem + TP_GO, tmem + d1c + 16 * s + 8, bh + ((s * 32) >> 4), ID_T_K64, 1);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1c, tmem + TP_XU + s * 8, bl + ((s * 32) >> 4), ID_T_K64, 1);
+          mma_bf16_ts_w(tmem + TP_GO, tmem + d1c + 16 * s, bl + ((s * 32) >> 4), ID_T_K64, 1);
         mma_commit_w(bar_g2);
       }
+      IPHASE(2);  // G2 issue
+      SEVENT(18);
       if (!last) {
         // ---- G1a_{c+1} = (g_c S_c) [K;Q]_{c+1}^T once the operand is stored -------------
-        ok = mbar_wait(bar_op, ph_op) && ok;
+        ok = mbar_wait_spin(bar_op, ph_op) && ok;
         ph_op ^= 1;
         tc_fence_after();
         __syncwarp();
         if (!ok) break;
+        IPHASE(3);  // operand wait
+        SEVENT(19);
+        // chunk c+2's K/Q tile into chunk c-1's buffer (the third one for c = 0): its
+        // last reader G3_{c-1} finished before this operand was signalled
+        if (leader && c + 2 < nch) issue_kq(c + 2);
+        __syncwarp();
         issue_g1a(d1n, kqn);
         mma_commit_w(bar_g1a);
+        IPHASE(4);  // G1a issue
+        SEVENT(20);
       }
       // ---- U'_c stored: G1'_c onto D1_{c+1}, then G3_c: dS_c = U'^T K_c ----------------
-      ok = mbar_wait(bar_u, ph_u) && ok;
+      ok = mbar_wait_spin(bar_u, ph_u) && ok;
+      IPHASE(5);  // U' wait
+      SEVENT(21);
       ph_u ^= 1;
       tc_fence_after();
       __syncwarp();
@@ -574,18 +617,17 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         const uint64_t bl = desc_kmajor(smem_u32(sm + Q_OFF_B + 16384));
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1n, tmem + TP_XU + s * 8, bh + ((s * 32) >> 4), ID_T_K, 1);
+          mma_bf16_ts_w(tmem + d1n, tmem + d1c + 16 * s, bh + ((s * 32) >> 4), ID_T_K, 1);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1n, tmem + TP_XU + 32 + s * 8, bh + ((s * 32) >> 4), ID_T_K64,
-                        1);
+          mma_bf16_ts_w(tmem + d1n, tmem + d1c + 16 * s + 8, bh + ((s * 32) >> 4), ID_T_K64, 1);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1n, tmem + TP_XU + s * 8, bl + ((s * 32) >> 4), ID_T_K64, 1);
+          mma_bf16_ts_w(tmem + d1n, tmem + d1c + 16 * s, bl + ((s * 32) >> 4), ID_T_K64, 1);
         mma_commit_w(bar_ch);
         // G3 overwrites the operand columns that G1a_{c+1} reads (another accumulator:
         // no implicit order between them)
-        ok = mbar_wait(bar_g1a, ph_g1a) && ok;
+        ok = mbar_wait_spin(bar_g1a, ph_g1a) && ok;
         ph_g1a ^= 1;
         tc_fence_after();
         __syncwarp();
@@ -595,19 +637,23 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         const uint64_t bk = desc_mnmajor(smem_u32(kqc), 16384);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + TP_S, tmem + TP_XU + s * 8, bk + ((s * 2048) >> 4), ID_T_MN,
+          mma_bf16_ts_w(tmem + TP_S, tmem + d1c + 16 * s, bk + ((s * 2048) >> 4), ID_T_MN,
                         s > 0);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + TP_S, tmem + TP_XU + 32 + s * 8, bk + ((s * 2048) >> 4), ID_T_MN,
+          mma_bf16_ts_w(tmem + TP_S, tmem + d1c + 16 * s + 8, bk + ((s * 2048) >> 4), ID_T_MN,
                         1);
         mma_commit_w(bar_g3);
       }
       // B_{c+1} for chunk c+1's state-side work (D1_c's buffer is read: U'_c is stored)
+      IPHASE(6);  // G1', G1a wait, G3
+      SEVENT(22);
       if (c + 2 < nch && !issue_b(c + 1)) {
         ok = false;
         break;
       }
+      IPHASE(7);  // B issue
+      SEVENT(23);
     }
   } else if (state_wg) {
     // ================================ state warps ======================================
@@ -623,11 +669,15 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
     };
     // the S operand: bf16 hi/lo of scale * S (this thread's 32 columns)
     auto write_s_operand = [&](float scale) {
-      uint32_t hw[16], lw[16];
+      float hl[32];  // bit images: 16 hi words, then 16 lo words
 #pragma unroll
-      for (int w = 0; w < 16; ++w) split2(scale * S[2 * w], scale * S[2 * w + 1], hw[w], lw[w]);
-      tmem_st16(lane + TP_S + 16 * ch, hw);
-      tmem_st16(lane + TP_S + 64 + 16 * ch, lw);
+      for (int w = 0; w < 16; ++w) {
+        uint32_t hw, lw;
+        split2(scale * S[2 * w], scale * S[2 * w + 1], hw, lw);
+        hl[w] = __uint_as_float(hw);
+        hl[16 + w] = __uint_as_float(lw);
+      }
+      tmem_st32(lane + TP_S + 32 * ch, hl);
       tmem_st_wait();
     };
     // prologue: the operand S_0 for D1_0
@@ -636,6 +686,21 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
 
     uint32_t ph_ch = 0, ph_g2 = 0, ph_tb = 0, ph_g3 = 0;
     float g_prev = 1.0f;  // gamma_last of the previous chunk
+    // output rows of the chunk (bf16 pairs), stored once U' is signalled
+    uint32_t opk[8];
+    int64_t o_cs = 0;
+    int o_L = 0;
+    auto store_output = [&]() {
+      __nv_bfloat16* dst = p.out + (o_cs * HV + h) * kHeadDim + v;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int ii = 16 * ch + i;
+        const uint32_t w = opk[i >> 1];
+        if (ii < o_L)
+          dst[static_cast<int64_t>(ii) * HV * kHeadDim] =
+              __ushort_as_bfloat16(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xffffu)));
+      }
+    };
 #ifdef GDN_PHASE_PROFILE
     long long sphase_last_ = clock64();
 #endif
@@ -650,47 +715,42 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       const float* sF = sGam + kC;
       const uint8_t* vt = sm + Q_OFF_V + b * 16384;
       SPHASE(0);
-      // ---- D1_c complete: X_c^T = V^T - (KH)^T diag(gamma); keep gamma (QH)^T --------
+      SEVENT(0);
+      // ---- D1_c complete: X_c^T = V^T - (KH)^T diag(gamma), over (KH)^T ------------------
       ok = mbar_wait(bar_ch, ph_ch) && ok;
       ph_ch ^= 1;
       ok = mbar_wait(&bar_va[b], static_cast<uint32_t>((c >> 1) & 1)) && ok;
       tc_fence_after();
       SPHASE(1);  // D1 wait
+      SEVENT(1);
       {
-        float d[16], qg[16];
+        float d[16];
         tmem_ld16(lane + d1c + 16 * ch, d);
-        tmem_ld16(lane + d1c + 64 + 16 * ch, qg);
         tmem_ld_wait();
         float x[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int j = 16 * ch + i;
-          const float gj = sGam[j];
           const unsigned short raw =
               *reinterpret_cast<const unsigned short*>(vt + j * 256 + v * 2);
-          x[i] = __uint_as_float(static_cast<uint32_t>(raw) << 16) - gj * d[i];
-          qg[i] *= gj;
+          x[i] = __uint_as_float(static_cast<uint32_t>(raw) << 16) - sGam[j] * d[i];
         }
         uint32_t hw[8], lw[8];
         split_words<8>(x, hw, lw);
-        if (c > 0) {  // G3_{c-1} has read U'_{c-1} and written dS_{c-1}
-          ok = mbar_wait(bar_g3, ph_g3) && ok;
-          ph_g3 ^= 1;
-          tc_fence_after();
-        }
-        tmem_st8(lane + TP_XU + 8 * ch, hw);
-        tmem_st8(lane + TP_XU + 32 + 8 * ch, lw);
-        uint32_t qw[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) qw[i] = __float_as_uint(qg[i]);
-        tmem_st16(lane + TP_QG + 16 * ch, qw);
+        tmem_st8(lane + d1c + 16 * ch, hw);
+        tmem_st8(lane + d1c + 16 * ch + 8, lw);
         tmem_st_wait();
       }
       signal(bar_x);
+      SEVENT(2);
       SPHASE(2);  // X build
 
       // ---- beside the chain: S_c = g_{c-1} S_{c-1} + dS_{c-1}; operand g_c S_c; B_c ------
       if (c > 0) {
+        ok = mbar_wait(bar_g3, ph_g3) && ok;  // G3_{c-1}: dS_{c-1}
+        ph_g3 ^= 1;
+        tc_fence_after();
+        SEVENT(11);
         float d0[32];
         tmem_ld32(lane + TP_S + 32 * ch, d0);
         tmem_ld_wait();
@@ -698,19 +758,23 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         for (int i = 0; i < 32; ++i) S[i] = fmaf(g_prev, S[i], d0[i]);
       }
       g_prev = sGam[kC - 1];
+      SEVENT(4);
       if (!last) {
         tc_fence_before();
         // every state thread has read dS_{c-1}
         if (!named_bar_and(kStateBar, kScanWState, ok)) break;
         tc_fence_after();
+        SEVENT(5);
         write_s_operand(g_prev);
+        SEVENT(6);
         ok = mbar_wait(bar_tb, ph_tb) && ok;
+        SEVENT(7);
         ph_tb ^= 1;
         tc_fence_after();
         {
           // row v of B_c^T (the [K;Q]_{c+1} row), columns i in [16c, 16c+16)
           float bt[16];
-          tmem_ld16(lane + d1n + 16 * ch, bt);
+          tmem_ld16(lane + d1n + 64 + 16 * ch, bt);
           tmem_ld_wait();
           uint32_t hw[8], lw[8];
           split_words<8>(bt, hw, lw);
@@ -727,40 +791,47 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
           }
         }
         signal(bar_op);
+        SEVENT(8);
       }
       SPHASE(3);  // state update, operand, B image
 
-      // ---- G2_c done: U'^T = U^T diag(f) (over X^T); output rows of chunk c -------------
+      // ---- G2_c done: U'^T = U^T diag(f) over X^T; output rows of chunk c ---------------
       ok = mbar_wait(bar_g2, ph_g2) && ok;
       ph_g2 ^= 1;
       tc_fence_after();
       SPHASE(4);  // G2 wait
+      SEVENT(9);
       {
-        float u[16], o[16];
-        tmem_ld16(lane + d1c + 16 * ch, u);
-        tmem_ld16(lane + d1c + 64 + 16 * ch, o);
+        float u[16];
+        tmem_ld16(lane + TP_GO + 16 * ch, u);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 16; ++i) u[i] *= sF[16 * ch + i];
         uint32_t hw[8], lw[8];
         split_words<8>(u, hw, lw);
-        tmem_st8(lane + TP_XU + 8 * ch, hw);
-        tmem_st8(lane + TP_XU + 32 + 8 * ch, lw);
-        tmem_st_wait();
-        signal(bar_u);
-        float qg[16];
-        tmem_ld16(lane + TP_QG + 16 * ch, qg);
+        tmem_st8(lane + d1c + 16 * ch, hw);
+        tmem_st8(lane + d1c + 16 * ch + 8, lw);
+        // O^T row v, tokens i in [16c, 16c+16): scale (gamma_i (QH)^T + (PX)^T); read before
+        // U' is signalled (B_{c+1} then overwrites the (QH)^T half)
+        float o[16], qv[16];
+        tmem_ld16(lane + TP_GO + 64 + 16 * ch, o);
+        tmem_ld16(lane + d1c + 64 + 16 * ch, qv);
         tmem_ld_wait();
-        __nv_bfloat16* dst = p.out + (cs * HV + h) * kHeadDim + v;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int ii = 16 * ch + i;
-          if (ii < L)
-            dst[static_cast<int64_t>(ii) * HV * kHeadDim] =
-                __float2bfloat16_rn(p.scale * (qg[i] + o[i]));
+        for (int i = 0; i < 8; ++i) {
+          const int i0 = 16 * ch + 2 * i;
+          opk[i] = pack2_rn(p.scale * fmaf(sGam[i0], qv[2 * i], o[2 * i]),
+                            p.scale * fmaf(sGam[i0 + 1], qv[2 * i + 1], o[2 * i + 1]));
         }
+        o_cs = cs;
+        o_L = L;
+        tmem_st_wait();
       }
-      SPHASE(5);  // U' and output
+      signal(bar_u);
+      SEVENT(10);
+      store_output();
+      SEVENT(3);
+      SPHASE(6);  // U' and output rows
     }
     if (ok) {
       ok = mbar_wait(bar_g3, ph_g3);
@@ -782,6 +853,9 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   if (!ok && p.status) atomicExch(p.status, 1);
   tc_fence_before();
   __syncthreads();
+#ifdef GDN_PHASE_PROFILE
+  if (blockIdx.x == 0 && t < 16) g_scan_cycles[t] += sprof_[t];
+#endif
   if (issuer) tmem_dealloc(tmem, kScanTTmemCols);
 }
 
@@ -874,6 +948,11 @@ extern "C" __attribute__((visibility("default"))) int gdn_debug_prep_cycles(long
     if (cudaMemcpyToSymbol(gdn::g_prep_cycles, z, sizeof(z)) != cudaSuccess) return -1;
   }
   return 0;
+}
+extern "C" __attribute__((visibility("default"))) int gdn_debug_scan_events(long long* host) {
+  return cudaMemcpyFromSymbol(host, gdn::g_scan_events, sizeof(long long) * 32) == cudaSuccess
+             ? 0
+             : -1;
 }
 extern "C" __attribute__((visibility("default"))) int gdn_debug_scan_cycles(long long* host,
                                                                               int reset) {

@@ -144,6 +144,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// Bounded wait without suspending: for a thread whose reaction time is on the critical
+// path (an MMA issuer); the same limits as mbar_wait.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_test_wait(addr, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test_wait(addr, parity)) return true;
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_async_smem() {
   // make generic-proxy writes to shared memory visible to the async proxy (MMA / TMA)
