@@ -291,7 +291,57 @@ def run_ours(args, world, rank, local):
             w: prefill_measure(w, k, 3, device, world, rank, peak=bf16_sus, peak_src=peak_src,
                                brief=True)
             for w, k in (("prefill_varlen", 10), ("prefill_long", 5))})
+        result["extra"]["decode_sweep"] = decode_sweep_measure(device, world, rank)
     return result
+
+
+def decode_sweep_measure(device, world, rank, batches=(1, 16, 64, 256, 1024, 4096)):
+    """Decode batch sweep (global batch B sharded by sequence over the ranks): per B, one
+    CUDA graph of R decode steps, each on its own state buffer (R chosen so that the
+    states of one replay exceed the L2 twice over; R = 1 once one state does), timed
+    with CUDA events over whole replays; max over ranks. Graph replay removes the
+    per-launch host cost that dominates B = 1 and 16."""
+    from flashinfer_bench_tma_thrust_b200 import decode, workloads as W
+    per_seq = HV * D * D * 4
+    out = []
+    for B in batches:
+        Bl = -(-B // world)
+        R = max(1, -(-(2 * 126 * 2 ** 20) // (Bl * per_seq)))
+        xs = [W.decode_inputs(Bl, seed=7000 + 31 * rank + r, gen_device=device, device=device)
+              for r in range(R)]
+        for x in xs:  # warm up outside the capture (library load, attribute set-up)
+            decode.kernel(*x.args())
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        keep = []
+        with torch.cuda.graph(g):
+            for x in xs:
+                keep.append(decode.kernel(*x.args()))
+        reps = max(3, min(200, int(2e8 // (R * Bl * per_seq * 2) + 1)))
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            g.replay()
+        e.record()
+        e.synchronize()
+        ms = s.elapsed_time(e)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        us_step = 1000.0 * ms / (reps * R)
+        out.append({"B": B, "B_per_gpu": Bl, "us_per_step": round(us_step, 2),
+                    "state_gbs": round(world * 2 * Bl * per_seq / (us_step * 1e-6) / 1e9, 1),
+                    "buffers_rotated": R})
+        del g, keep, xs
+        torch.cuda.empty_cache()
+    return out
 
 
 def decode_bf16_measure(x, info, K, Wm, device, world, fp32_ms_step):
