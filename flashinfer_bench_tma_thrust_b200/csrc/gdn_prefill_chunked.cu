@@ -93,8 +93,7 @@ __device__ long long g_phase_cycles[16];
 __global__ void __launch_bounds__(128, 2)
     prefill_chunked_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                           ~uintptr_t(1023));
+  uint8_t* sm = align_smem<1024>(smem_raw);
   float* sAf = reinterpret_cast<float*>(sm + OFF_AF);  // (aliases H hi, see the map)
   float* sTf = reinterpret_cast<float*>(sm + OFF_TF);
   float* sG = reinterpret_cast<float*>(sm + OFF_G);

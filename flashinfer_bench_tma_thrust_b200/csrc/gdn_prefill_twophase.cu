@@ -193,8 +193,7 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
     prep_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
                 const int64_t* __restrict__ offs, uint8_t* __restrict__ a2_out) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                           ~uintptr_t(1023));
+  uint8_t* sm = align_smem<1024>(smem_raw);
   float* sAf = reinterpret_cast<float*>(sm + P_OFF_AF);
   float* sTf = reinterpret_cast<float*>(sm + P_OFF_TF);
   float* sG = reinterpret_cast<float*>(sm + P_OFF_G);
@@ -396,8 +395,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
                   const int64_t* __restrict__ offs, const int32_t* __restrict__ order,
                   const uint8_t* __restrict__ a2_in) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                           ~uintptr_t(1023));
+  uint8_t* sm = align_smem<1024>(smem_raw);
   uint64_t* bar_kq = reinterpret_cast<uint64_t*>(sm + Q_OFF_BAR);  // [3] K/Q tiles
   uint64_t* bar_va = bar_kq + 3;                                   // [2] V + [T_b; P]
   uint64_t* bar_g2 = bar_kq + 5;    // commits: G2

@@ -18,8 +18,7 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
                                                             const __nv_bfloat16* B, float* D,
                                                             int a_mn, int b_mn, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   uint8_t* sA = smem;            // 32 KB
   uint8_t* sB = smem + 32768;    // 16 KB
   __shared__ uint64_t bar;
@@ -93,8 +92,7 @@ __global__ void __launch_bounds__(128) umma_ts_selftest_kernel(const __nv_bfloat
                                                                const __nv_bfloat16* B, float* D,
                                                                int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   uint8_t* sB = smem;  // 2 k-halves x 128 rows (n) x 128 B = 32 KB
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;

@@ -30,6 +30,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 // ---------------------------------------------------------------- swizzled tile addressing
 // Byte offset of element (row, col) (2-byte elements) inside a 128B-swizzled tile.
+// Dynamic shared memory rounded up to kAlign bytes, by pointer arithmetic on the shared
+// array itself: accesses through the result stay shared-memory accesses (a round trip
+// through an integer type would leave only a generic pointer, and every access through
+// it a generic load or store).
+template <uint32_t kAlign>
+__device__ __forceinline__ uint8_t* align_smem(uint8_t* raw) {
+  const uint32_t a = smem_u32(raw);
+  return raw + ((kAlign - (a & (kAlign - 1))) & (kAlign - 1));
+}
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
   return row * 128u + ((((col >> 3) ^ row) & 7u) << 4) + ((col & 7u) << 1);
 }
