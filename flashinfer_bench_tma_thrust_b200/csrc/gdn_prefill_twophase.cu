@@ -376,7 +376,7 @@ constexpr uint32_t Q_OFF_A2 = 98304;      // 2 x 24 KB: [T_b; P] hi 16 KB | T_b 
 constexpr uint32_t Q_OFF_V = 147456;      // 2 x 16 KB: V tile, rows j x 128 v
 constexpr uint32_t Q_OFF_B = 180224;      // B_c^T image: hi 16 KB (128 rows) | lo 8 KB (K rows)
 constexpr uint32_t Q_OFF_GATES = 204800;  // 2 x (gamma_j, f_j): 2 x 512 B, from the prep
-constexpr uint32_t Q_OFF_BAR = 206848;    // 13 mbarriers, TMEM slot
+constexpr uint32_t Q_OFF_BAR = 206848;    // 14 mbarriers, TMEM slot
 constexpr uint32_t Q_OFF_PROF = 206848 + 256;  // debug phase timers (16 x 8 B)
 constexpr uint32_t kScanWSmem = 206848 + 512 + 1024;
 // operand g S: thread quarter c writes columns [32c, 32c + 32) as 16 hi words then 16 lo
@@ -404,8 +404,9 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   uint64_t* bar_g3 = bar_kq + 8;    //          G3
   uint64_t* bar_g1a = bar_kq + 9;   //          G1a
   uint64_t* bar_x = bar_kq + 10;    // state warps: X^T stored
-  uint64_t* bar_op = bar_kq + 11;   //              S operand and B_c image stored
+  uint64_t* bar_op = bar_kq + 11;   //              S operand stored
   uint64_t* bar_u = bar_kq + 12;    //              U'^T stored
+  uint64_t* bar_bi = bar_kq + 13;   //              B_c image stored
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Q_OFF_BAR + 128);
 #ifdef GDN_PHASE_PROFILE
   long long* sprof_ = reinterpret_cast<long long*>(sm + Q_OFF_PROF);
@@ -445,7 +446,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
 
   if (t == 0) {
     for (int i = 0; i < 10; ++i) mbar_init(&bar_kq[i], 1);
-    for (int i = 10; i < 13; ++i) mbar_init(&bar_kq[i], kScanWState / 32);
+    for (int i = 10; i < 14; ++i) mbar_init(&bar_kq[i], kScanWState / 32);
     fence_mbar_init();
   }
   if (issuer) tmem_alloc(tmem_slot, kScanTTmemCols);
@@ -530,7 +531,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       }
     }
     __syncwarp();
-    uint32_t ph_x = 0, ph_op = 0, ph_u = 0, ph_g1a = 0;
+    uint32_t ph_x = 0, ph_op = 0, ph_u = 0, ph_bi = 0, ph_g1a = 0;
     // prologue: D1_0 = S_0 [K;Q]_0^T
     ok = mbar_wait_spin(bar_op, ph_op) && ok;
     ph_op ^= 1;
@@ -611,6 +612,11 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       __syncwarp();
       if (!ok) break;
       if (!last) {
+        ok = mbar_wait_spin(bar_bi, ph_bi) && ok;  // the B_c image
+        ph_bi ^= 1;
+        tc_fence_after();
+        __syncwarp();
+        if (!ok) break;
         const uint64_t bh = desc_kmajor(smem_u32(sm + Q_OFF_B));
         const uint64_t bl = desc_kmajor(smem_u32(sm + Q_OFF_B + 16384));
 #pragma unroll
@@ -764,6 +770,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         tc_fence_after();
         SEVENT(5);
         write_s_operand(g_prev);
+        signal(bar_op);
         SEVENT(6);
         ok = mbar_wait(bar_tb, ph_tb) && ok;
         SEVENT(7);
@@ -788,7 +795,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
                 make_uint4(lw[4], lw[5], lw[6], lw[7]);
           }
         }
-        signal(bar_op);
+        signal(bar_bi);
         SEVENT(8);
       }
       SPHASE(3);  // state update, operand, B image
