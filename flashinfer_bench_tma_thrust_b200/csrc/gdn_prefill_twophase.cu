@@ -169,27 +169,28 @@ __global__ void __launch_bounds__(256) scan_order_kernel(int64_t N, const int64_
 }
 
 // ------------------------------------------------------------------ prep
-// 256 threads; thread t owns TMEM lane / row t % 128 and a 32-column half of it.
-// Shared memory: the K/Q tile (32 KB, TMA) is dead after S and then holds the fp32 A
-// and T of the solve (padded rows, 17 KB each), then T_b hi/lo over A. M hi/lo (rows
-// 0..63 of the A operand of P = M T_b; the operand's rows 64..127 read whatever
-// follows — those result rows are not used).
+// 256 threads; thread t owns TMEM lane / row t % 128 and a 32-column half of it. Four
+// blocks per SM (64 registers, 52 KB of shared memory, 128 TMEM columns each).
+// Shared memory: the K/Q tile (32 KB, TMA) is dead after S; then M hi/lo (rows 0..63 of
+// the A operand of P = M T_b: the operand reads 128 rows, the rows after M lo are A's
+// and their results are not used), the fp32 A and T of the solve (padded rows, 17 KB
+// each), and T_b hi/lo over A once the solve no longer reads it.
 constexpr uint32_t P_OFF_KQ = 0;
-constexpr uint32_t P_OFF_AF = 0;
-constexpr uint32_t P_OFF_TF = 17408;
-constexpr uint32_t P_OFF_TB_HI = 0;
-constexpr uint32_t P_OFF_TB_LO = 8192;
-constexpr uint32_t P_OFF_M_HI = 35840;   // 1024-aligned, after T
-constexpr uint32_t P_OFF_M_LO = 44032;   // rows 64..127 of the hi operand = these rows
-constexpr uint32_t P_OFF_G = 60416;      // (52224..60416: rows 64..127 of the lo operand)
-constexpr uint32_t P_OFF_BETA = 60672;
-constexpr uint32_t P_OFF_BAR = 60928;
-constexpr uint32_t kPrepSmem = 60992 + 1024;
+constexpr uint32_t P_OFF_M_HI = 0;
+constexpr uint32_t P_OFF_M_LO = 8192;
+constexpr uint32_t P_OFF_AF = 16384;
+constexpr uint32_t P_OFF_TF = 33792;
+constexpr uint32_t P_OFF_TB_HI = 16384;
+constexpr uint32_t P_OFF_TB_LO = 24576;
+constexpr uint32_t P_OFF_G = 51200;
+constexpr uint32_t P_OFF_BETA = 51456;
+constexpr uint32_t P_OFF_BAR = 51712;
+constexpr uint32_t kPrepSmem = 51776 + 1024;
 constexpr uint32_t kPrepTmemCols = 128;
 constexpr uint32_t PT_S = 0, PT_P = 64;
 constexpr int kPrepThreads = 256;
 
-__global__ void __launch_bounds__(kPrepThreads, 3)
+__global__ void __launch_bounds__(kPrepThreads, 4)
     prep_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
                 const int64_t* __restrict__ offs, uint8_t* __restrict__ a2_out) {
   extern __shared__ uint8_t smem_raw[];
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kPrepThreads, 3)
     tc_fence_after();
     PPHASE(2);  // S MMA
     if (__syncthreads_and(ok)) {
-      // the K/Q tile is dead: A, T and T_b reuse its space
+      // the K/Q tile is dead: M and A reuse its space
       build_a_m_256<PadLayout>(trow + PT_S, sAf, sG, sBeta, sm + P_OFF_M_HI, sm + P_OFF_M_LO);
       __syncthreads();
       PPHASE(3);  // build A, M
