@@ -378,7 +378,9 @@ constexpr uint32_t Q_OFF_V = 147456;      // 2 x 16 KB: V tile, rows j x 128 v
 constexpr uint32_t Q_OFF_B = 180224;      // B_c^T image: hi 16 KB (128 rows) | lo 8 KB (K rows)
 constexpr uint32_t Q_OFF_GATES = 204800;  // 2 x (gamma_j, f_j): 2 x 512 B, from the prep
 constexpr uint32_t Q_OFF_BAR = 206848;    // 14 mbarriers, TMEM slot
+#ifdef GDN_PHASE_PROFILE
 constexpr uint32_t Q_OFF_PROF = 206848 + 256;  // debug phase timers (16 x 8 B)
+#endif
 constexpr uint32_t kScanWSmem = 206848 + 512 + 1024;
 // operand g S: thread quarter c writes columns [32c, 32c + 32) as 16 hi words then 16 lo
 // words (K step s: hi at 32 (s/2) + 8 (s%2), lo 16 further); dS (fp32) from G3

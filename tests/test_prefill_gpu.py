@@ -29,6 +29,7 @@ def test_prefill_matches_reference_golden(name, impl):
 LENGTHS = [
     [1], [63], [64], [65], [128], [200, 0, 1, 64, 127],
     [0, 0], [300, 17],
+    [129, 192, 193, 256],  # 3-4 chunks: the pipelined scan's prologue, steady state, tail
 ]
 
 
@@ -86,6 +87,17 @@ def test_chunked_vs_recurrent_varlen_config():
     assert_state_close(s1, s2, PREFILL_STATE_ATOL, "chunked vs recurrent")
     assert_out_close(o3, o2, "fused vs recurrent")
     assert_state_close(s3, s2, PREFILL_STATE_ATOL, "fused vs recurrent")
+
+
+def test_chunked_vs_recurrent_long_sequence():
+    """Config 5's sequence length (32,768 tokens = 512 chunks) plus a ragged second
+    sequence: the chunk-64 path stays within the parity tolerances of the token-by-token
+    fp32 recurrence over the whole length (a size-independent check at full size)."""
+    x = W.prefill_inputs([32768, 1000], seed=77, gen_device="cuda", device="cuda")
+    o1, s1 = prefill.kernel(*x.args())
+    o2, s2 = prefill.kernel_recurrent(*x.args())
+    assert_out_close(o1, o2, "chunked vs recurrent, 32768 tokens")
+    assert_state_close(s1, s2, PREFILL_STATE_ATOL, "chunked vs recurrent, 32768 tokens")
 
 
 def test_chunked_status_word_clean():
