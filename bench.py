@@ -75,28 +75,70 @@ def ncu_traffic(key: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    """SM clock and throttle-reason sampling during the timed region: NVML polled from a
+    background thread about every millisecond (so that even a few-millisecond region gets
+    samples; the first sample is taken before the constructor returns), else nvidia-smi
+    at its 50 ms minimum. Reads only; changes no GPU setting."""
 
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, device: torch.device):
+        import threading
         self.proc = None
         self.file = None
+        self.thread = None
+        self.sm, self.reasons, self.max_mhz = [], set(), None
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+        self.uuid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
         try:
-            uuid = str(torch.cuda.get_device_properties(device).uuid)
-            sel = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByUUID(self.uuid)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.stop_flag = threading.Event()
+            first = threading.Event()
+
+            def poll():
+                while True:
+                    self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                    bits = int(get_reasons(h))
+                    for name, bit in self.BITS.items():
+                        if bits & bit:
+                            self.reasons.add(name)
+                    first.set()
+                    if self.stop_flag.wait(0.001):
+                        break
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            first.wait(5.0)
+            return
+        except Exception:
+            self.thread = None
+        try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", sel, f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            sm = list(self.sm)
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(self.reasons), "samples": len(sm), "source": "nvml"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
         self.proc.terminate()
@@ -120,7 +162,7 @@ class ClockSampler:
                 if val.strip() == "Active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------------- workloads
