@@ -105,8 +105,8 @@ _workspaces: dict = {}
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Per-device workspace of the chunked prefill (zeroed once; its first bytes hold
-    the sticky status word, the rest the per-chunk [T_b; P] operands of the two-phase
-    path, 24 KB per (chunk, v-head)). Grown on demand, never shrunk; calls on one
+    the sticky status word, the rest the per-chunk units of the two-phase path: the
+    [T_b; P] operand image and the chunk's gates, 24.5 KB per (chunk, v-head)). Grown on demand, never shrunk; calls on one
     device share it, so they must be ordered on one stream."""
     key = (device.type, device.index)
     ws = _workspaces.get(key)

@@ -155,16 +155,18 @@ GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* 
  *                    before its first use. With at least
  *                    gdn_prefill_chunked_workspace_size(T, N, HV) bytes the call
  *                    runs the two-phase path (a parallel prep kernel over all
- *                    (chunk, v-head) pairs writes 24 KB per pair, then the state
- *                    scan); with less, but at least 256 bytes, it runs the fused
+ *                    (chunk, v-head) pairs writes 24.5 KB per pair — the [T_b; P]
+ *                    operand image and the chunk's gates — then the state scan);
+ *                    with less, but at least 256 bytes, it runs the fused
  *                    single-kernel path. The first 4 bytes are a sticky status
  *                    word that a kernel sets to 1 if one of its bounded waits gave
  *                    up (read it with gdn_prefill_chunked_status). Calls that
  *                    share a workspace must be stream-ordered.
  *
  * q, k, v and out must be 16-byte aligned (q/k are read by TMA); T < 2^31.
- * One launch per call; the work runs in fp32 on the state with tensor-core
- * products carried as bf16 hi/lo pairs (about 16 significant bits).
+ * Stream-ordered launches, no host synchronisation (two-phase path: chunk offsets,
+ * scan order, prep, scan; fused path: one kernel); the work runs in fp32 on the state
+ * with tensor-core products carried as bf16 hi/lo pairs (about 16 significant bits).
  */
 GDN_API size_t gdn_prefill_chunked_workspace_size(int64_t T, int64_t N, int32_t HV);
 
