@@ -375,17 +375,24 @@ __device__ __forceinline__ void build_a_m_256(uint32_t ts_row, float* sAf, const
     for (int j = 0; j < 32; j += 4) {
       float4 w;
       const int jj = c0 + j;
-      w.x = (jj + 0 < r) ? bi * ex2(gi - sG[jj + 0]) * srow[j + 0] : 0.f;
-      w.y = (jj + 1 < r) ? bi * ex2(gi - sG[jj + 1]) * srow[j + 1] : 0.f;
-      w.z = (jj + 2 < r) ? bi * ex2(gi - sG[jj + 2]) * srow[j + 2] : 0.f;
-      w.w = (jj + 3 < r) ? bi * ex2(gi - sG[jj + 3]) * srow[j + 3] : 0.f;
+      const float4 g = *reinterpret_cast<const float4*>(sG + jj);
+      w.x = (jj + 0 < r) ? bi * ex2(gi - g.x) * srow[j + 0] : 0.f;
+      w.y = (jj + 1 < r) ? bi * ex2(gi - g.y) * srow[j + 1] : 0.f;
+      w.z = (jj + 2 < r) ? bi * ex2(gi - g.z) * srow[j + 2] : 0.f;
+      w.w = (jj + 3 < r) ? bi * ex2(gi - g.w) * srow[j + 3] : 0.f;
       *reinterpret_cast<float4*>(sAf + Lay::idx(r, jj)) = w;
     }
   } else {
     const int i = r - kC;
     const float gi = sG[i];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) srow[j] = (c0 + j <= i) ? ex2(gi - sG[c0 + j]) * srow[j] : 0.f;
+    for (int j = 0; j < 32; j += 4) {
+      const float4 g = *reinterpret_cast<const float4*>(sG + c0 + j);
+      srow[j] = (c0 + j <= i) ? ex2(gi - g.x) * srow[j] : 0.f;
+      srow[j + 1] = (c0 + j + 1 <= i) ? ex2(gi - g.y) * srow[j + 1] : 0.f;
+      srow[j + 2] = (c0 + j + 2 <= i) ? ex2(gi - g.z) * srow[j + 2] : 0.f;
+      srow[j + 3] = (c0 + j + 3 <= i) ? ex2(gi - g.w) * srow[j + 3] : 0.f;
+    }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t hw[4], lw[4];
@@ -491,12 +498,13 @@ __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float
     for (int c = 0; c < 16; c += 4) {
       const int nn = qq * 16 + c;
       const float4 tv = *reinterpret_cast<const float4*>(sTf + Lay::idx(j, nn));
-      const float tvs[4] = {tv.x, tv.y, tv.z, tv.w};
+      const float4 bv = *reinterpret_cast<const float4*>(sBeta + nn);
+      const float tvs[4] = {tv.x * bv.x, tv.y * bv.y, tv.z * bv.z, tv.w * bv.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int m = nn + e;
         const bool lower = (m >> 4) < (j >> 4) || ((m >> 4) == (j >> 4) && m <= j);
-        vals[c + e] = lower ? tvs[e] * sBeta[m] : 0.f;
+        vals[c + e] = lower ? tvs[e] : 0.f;
       }
     }
 #pragma unroll
