@@ -342,6 +342,112 @@ __device__ __forceinline__ void split_words(const float* x, uint32_t (&hi)[NW], 
   for (int w = 0; w < NW; ++w) split2(x[2 * w], x[2 * w + 1], hi[w], lo[w]);
 }
 
+// ------------------------------------------------------------------ scan: MMA groups
+// Each group of the scan's products is issued from one asm block: one elect.sync, the
+// accumulate predicates set once, the per-K-step operand offsets as immediates. The
+// issuing warp shares its SM sub-partition with four busy state warps; with fewer
+// instructions per MMA the group is issued faster when the sub-partition's issue slots
+// are contended (a micro-benchmark with four FMA-bound warps beside the issuer: 2.0 K
+// cycles for the 16-MMA group against 3.1 K with one elect.sync per MMA). Called by all
+// lanes of the issuing warp.
+
+// G1a: D (128 x 128) = A^T-operand in TMEM (thread quarter layout: K step s hi at
+// 32 (s/2) + 8 (s%2), lo 16 further) x K-major B tile with two 64-wide K atoms
+// (16 KB apart): 8 hi steps at N = 128, 8 lo steps at N = 64.
+__device__ __forceinline__ void mma_group_g1a(uint32_t d, uint32_t a, uint64_t b) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 bb;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 pf, 0, 0;\n\tsetp.eq.b32 pt, 0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pf;\n\t"
+      "add.s64 bb, %2, 2;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 4;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 6;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 1024;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 1026;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 1028;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%10], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 1030;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%11], bb, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%12], %2, %4, pt;\n\t"
+      "add.s64 bb, %2, 2;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%13], bb, %4, pt;\n\t"
+      "add.s64 bb, %2, 4;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%14], bb, %4, pt;\n\t"
+      "add.s64 bb, %2, 6;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%15], bb, %4, pt;\n\t"
+      "add.s64 bb, %2, 1024;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%16], bb, %4, pt;\n\t"
+      "add.s64 bb, %2, 1026;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%17], bb, %4, pt;\n\t"
+      "add.s64 bb, %2, 1028;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%18], bb, %4, pt;\n\t"
+      "add.s64 bb, %2, 1030;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%19], bb, %4, pt;\n\t"
+      "}" ::"r"(d), "r"(a), "l"(b), "r"(ID_T_K), "r"(ID_T_K64), "r"(a + 8), "r"(a + 32),
+      "r"(a + 40), "r"(a + 64), "r"(a + 72), "r"(a + 96), "r"(a + 104), "r"(a + 16),
+      "r"(a + 24), "r"(a + 48), "r"(a + 56), "r"(a + 80), "r"(a + 88), "r"(a + 112),
+      "r"(a + 120)
+      : "memory");
+}
+
+// G2 / G1': D = A x B over a 64-deep K: A in TMEM with each 16-column group holding one
+// K step's hi (columns 0..7) and lo (8..15); B a K-major tile (hi; lo for the first 64
+// rows only). Three-term split product: 4 x (hi hi, N = 128), 4 x (lo hi, N = 64),
+// 4 x (hi lo, N = 64). `acc` = accumulate onto D from the first MMA.
+__device__ __forceinline__ void mma_group_x3(uint32_t d, uint32_t a, uint64_t bh, uint64_t bl,
+                                             uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p0, pt;\n\t.reg .b64 bb;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p0, %5, 0;\n\tsetp.eq.b32 pt, 0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %6, p0;\n\t"
+      "add.s64 bb, %2, 2;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], bb, %6, pt;\n\t"
+      "add.s64 bb, %2, 4;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], bb, %6, pt;\n\t"
+      "add.s64 bb, %2, 6;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%10], bb, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%11], %2, %7, pt;\n\t"
+      "add.s64 bb, %2, 2;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%12], bb, %7, pt;\n\t"
+      "add.s64 bb, %2, 4;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%13], bb, %7, pt;\n\t"
+      "add.s64 bb, %2, 6;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%14], bb, %7, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %7, pt;\n\t"
+      "add.s64 bb, %3, 2;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], bb, %7, pt;\n\t"
+      "add.s64 bb, %3, 4;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], bb, %7, pt;\n\t"
+      "add.s64 bb, %3, 6;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%10], bb, %7, pt;\n\t"
+      "}" ::"r"(d), "r"(a), "l"(bh), "l"(bl), "r"(0u), "r"(acc), "r"(ID_T_K), "r"(ID_T_K64),
+      "r"(a + 16), "r"(a + 32), "r"(a + 48), "r"(a + 8), "r"(a + 24), "r"(a + 40), "r"(a + 56)
+      : "memory");
+}
+
+// G3: D (128 x 128) = A (layout of mma_group_x3) x MN-major K tile (2048 B per K step):
+// 4 x hi, 4 x lo, N = 128, the first MMA overwriting D.
+__device__ __forceinline__ void mma_group_g3(uint32_t d, uint32_t a, uint64_t b) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 bb;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 pf, 0, 0;\n\tsetp.eq.b32 pt, 0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pf;\n\t"
+      "add.s64 bb, %2, 128;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 256;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 384;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], bb, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %2, %3, pt;\n\t"
+      "add.s64 bb, %2, 128;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 256;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], bb, %3, pt;\n\t"
+      "add.s64 bb, %2, 384;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%10], bb, %3, pt;\n\t"
+      "}" ::"r"(d), "r"(a), "l"(b), "r"(ID_T_MN), "r"(a + 16), "r"(a + 32), "r"(a + 48),
+      "r"(a + 8), "r"(a + 24), "r"(a + 40), "r"(a + 56)
+      : "memory");
+}
+
+// B_m^T = [K;Q]_{m+1} K_m^T: 8 shared-memory x shared-memory steps (K-major, two K atoms
+// 16 KB apart), N = 64, the first MMA overwriting D.
+__device__ __forceinline__ void mma_group_b(uint32_t d, uint64_t a, uint64_t b) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 aa, bb;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 pf, 0, 0;\n\tsetp.eq.b32 pt, 0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, pf;\n\t"
+      "add.s64 aa, %1, 2;\n\tadd.s64 bb, %2, 2;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], aa, bb, %3, pt;\n\t"
+      "add.s64 aa, %1, 4;\n\tadd.s64 bb, %2, 4;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], aa, bb, %3, pt;\n\t"
+      "add.s64 aa, %1, 6;\n\tadd.s64 bb, %2, 6;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], aa, bb, %3, pt;\n\t"
+      "add.s64 aa, %1, 1024;\n\tadd.s64 bb, %2, 1024;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], aa, bb, %3, pt;\n\t"
+      "add.s64 aa, %1, 1026;\n\tadd.s64 bb, %2, 1026;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], aa, bb, %3, pt;\n\t"
+      "add.s64 aa, %1, 1028;\n\tadd.s64 bb, %2, 1028;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], aa, bb, %3, pt;\n\t"
+      "add.s64 aa, %1, 1030;\n\tadd.s64 bb, %2, 1030;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], aa, bb, %3, pt;\n\t"
+      "}" ::"r"(d), "l"(a), "l"(b), "r"(ID_KK)
+      : "memory");
+}
+
 // ------------------------------------------------------------------ scan, pipelined
 // The state product of chunk c+1 is split so that most of it leaves the chain:
 // with S_{c+1} = g_c S_c + U'_c^T K_c (g_c = gamma_last of chunk c),
@@ -496,15 +602,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
     };
     // G1a: D1 (columns d) = (operand columns) [K;Q]^T of the tile kq
     auto issue_g1a = [&](uint32_t d, const uint8_t* kq) {
-      const uint64_t bd = desc_kmajor(smem_u32(kq));
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-        mma_bf16_ts_w(tmem + d, tmem + TP_S + 32 * (s >> 1) + 8 * (s & 1),
-                      bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K, s > 0);
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-        mma_bf16_ts_w(tmem + d, tmem + TP_S + 32 * (s >> 1) + 16 + 8 * (s & 1),
-                      bd + (((s >> 2) * 16384 + (s & 3) * 32) >> 4), ID_T_K64, 1);
+      mma_group_g1a(tmem + d, tmem + TP_S, desc_kmajor(smem_u32(kq)));
     };
     // B_m^T = [K;Q]_{m+1} K_m^T (exact bf16 operands, one term) into the first 64
     // columns of D1_{m+1}'s buffer (free until G1a_{m+1})
@@ -515,13 +613,8 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       if (!w) return false;
       const uint8_t* kqm = sm + Q_OFF_KQ + static_cast<int>(m % 3) * 32768;
       const uint8_t* kqm1 = sm + Q_OFF_KQ + static_cast<int>((m + 1) % 3) * 32768;
-      const uint64_t an = desc_kmajor(smem_u32(kqm1)), bc = desc_kmajor(smem_u32(kqm));
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint64_t off = ((s >> 2) * 16384 + (s & 3) * 32) >> 4;
-        mma_bf16_w(tmem + TP_D1 + 128 * static_cast<uint32_t>((m + 1) & 1) + 64, an + off,
-                   bc + off, ID_KK, s > 0);
-      }
+      mma_group_b(tmem + TP_D1 + 128 * static_cast<uint32_t>((m + 1) & 1) + 64,
+                  desc_kmajor(smem_u32(kqm1)), desc_kmajor(smem_u32(kqm)));
       mma_commit_w(bar_tb);
       return true;
     };
@@ -574,16 +667,8 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       IPHASE(1);  // X wait
       SEVENT(17);
       {
-        const uint64_t bh = desc_kmajor(smem_u32(a2)), bl = desc_kmajor(smem_u32(a2 + 16384));
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + TP_GO, tmem + d1c + 16 * s, bh + ((s * 32) >> 4), ID_T_K, s > 0);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + TP_GO, tmem + d1c + 16 * s + 8, bh + ((s * 32) >> 4), ID_T_K64, 1);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + TP_GO, tmem + d1c + 16 * s, bl + ((s * 32) >> 4), ID_T_K64, 1);
+        mma_group_x3(tmem + TP_GO, tmem + d1c, desc_kmajor(smem_u32(a2)),
+                     desc_kmajor(smem_u32(a2 + 16384)), 0u);
         mma_commit_w(bar_g2);
       }
       IPHASE(2);  // G2 issue
@@ -620,17 +705,8 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         tc_fence_after();
         __syncwarp();
         if (!ok) break;
-        const uint64_t bh = desc_kmajor(smem_u32(sm + Q_OFF_B));
-        const uint64_t bl = desc_kmajor(smem_u32(sm + Q_OFF_B + 16384));
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1n, tmem + d1c + 16 * s, bh + ((s * 32) >> 4), ID_T_K, 1);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1n, tmem + d1c + 16 * s + 8, bh + ((s * 32) >> 4), ID_T_K64, 1);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + d1n, tmem + d1c + 16 * s, bl + ((s * 32) >> 4), ID_T_K64, 1);
+        mma_group_x3(tmem + d1n, tmem + d1c, desc_kmajor(smem_u32(sm + Q_OFF_B)),
+                     desc_kmajor(smem_u32(sm + Q_OFF_B + 16384)), 1u);
         mma_commit_w(bar_ch);
         // G3 overwrites the operand columns that G1a_{c+1} reads (another accumulator:
         // no implicit order between them)
@@ -641,15 +717,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         if (!ok) break;
       }
       {
-        const uint64_t bk = desc_mnmajor(smem_u32(kqc), 16384);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + TP_S, tmem + d1c + 16 * s, bk + ((s * 2048) >> 4), ID_T_MN,
-                        s > 0);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_ts_w(tmem + TP_S, tmem + d1c + 16 * s + 8, bk + ((s * 2048) >> 4), ID_T_MN,
-                        1);
+        mma_group_g3(tmem + TP_S, tmem + d1c, desc_mnmajor(smem_u32(kqc), 16384));
         mma_commit_w(bar_g3);
       }
       // B_{c+1} for chunk c+1's state-side work (D1_c's buffer is read: U'_c is stored)
