@@ -161,28 +161,6 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// chunk_gates for warps 0 and 1 only (threads 0..63), synchronised with a named
-// barrier so that the other warps can work meanwhile. Readers of sG / sBeta in
-// other warps must pass a block-wide barrier afterwards.
-__device__ __forceinline__ void chunk_gates_w01(float ra, float rb, int L, float A_log,
-                                                float dtb, float* sG, float* sBeta,
-                                                int base = 0, uint32_t bar_id = 1) {
-  // the two warps are threads [base, base + 64); token index t = thread - base
-  const int t = threadIdx.x - base, lane = t & 31;
-  const bool valid = t < L;
-  const float lg = valid ? gate_log_decay(A_log, ra, dtb) * kLog2e : 0.0f;
-  const float beta = valid ? gate_beta(rb) : 0.0f;
-  float x = lg;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (t < 32) sG[t] = x;
-  sBeta[t] = beta;
-  named_bar_sync(bar_id, 64);
-  if (t >= 32) sG[t] = x + sG[31];
-}
 
 // From S = [K;Q] K^T in TMEM (this thread's lane): thread t < 64 writes row t of
 // A = strict_lower(beta_i e^{Gamma_i-Gamma_j} S_kk) (fp32, for the solve) and the

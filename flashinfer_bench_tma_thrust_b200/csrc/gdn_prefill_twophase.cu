@@ -332,7 +332,7 @@ constexpr uint32_t ID_T_MN = idesc_bf16(128, 128, false, true);   // B MN-major
 constexpr uint32_t ID_T_K64 = idesc_bf16(128, 64, false, false);
 
 struct ScanMaps {
-  CUtensorMap k, q, v, o;
+  CUtensorMap k, q, v;
 };
 
 // 2n fp32 -> n bf16x2 words, hi and lo parts
@@ -457,26 +457,18 @@ __device__ __forceinline__ void mma_group_b(uint32_t d, uint64_t a, uint64_t b) 
 // so the chain of one chunk is X_c -> G2_c -> U'_c -> G1'_c -> X_{c+1}; G1a_{c+1}, the
 // state product G3_c (dS_c = U'_c^T K_c), the state update and B_c = [K;Q]_{c+1} K_c^T
 // (exact bf16 operands) run beside it. G2_c writes its [U^T | (PX)^T] over D1_c
-// (gamma (QH)^T is parked in TMEM for the output).
+// (the (QH)^T half of D1_c is read for the output before G2's result is consumed).
 //
-// Warp roles: warps 0-15 (warpgroups 0-3, 512 threads) own the state: thread t holds
-// row v = t % 128 and quarter c = t / 128 of every row-sliced quantity (32 state
-// columns, 16 columns of X / U / output), and compute everything on CUDA cores; warp 16
-// (warpgroup 4, whose other warps idle) issues every MMA and every copy and does
-// nothing else, so that an issue that blocks on a full MMA queue never delays the
-// state warps. Registers: launched with kScanWLaunchRegs per thread; warpgroup 4 gives
-// its share down to kScanWIssuerRegs and the state warpgroups take kScanWStateRegs
-// (4 x 128 x 104 + 128 x 56 <= 640 x 96: the split must not exceed the launch total). The state warps tell the issuer that an
-// operand is ready through mbarriers (one arrival per warp); the issuer's commits
-// tell the state warps that a product is done.
-constexpr int kScanWThreads = 640;
+// Warp roles: warps 0-15 (512 threads) own the state: thread t holds row v = t % 128
+// and quarter c = t / 128 of every row-sliced quantity (32 state columns, 16 columns of
+// X / U / output), and compute everything on CUDA cores; warp 16 issues every MMA and
+// every copy and does nothing else, so that an issue that blocks on a full MMA queue
+// never delays the state warps. 96 registers per thread (17 warps: at most five share
+// an SM sub-partition's register file). The state warps tell the issuer that an
+// operand is ready through mbarriers (one arrival per warp); the issuer's commits tell
+// the state warps that a product is done.
+constexpr int kScanWThreads = 544;
 constexpr int kScanWState = 512;          // state threads (warps 0-15)
-constexpr uint32_t kScanWLaunchRegs = 96;
-constexpr uint32_t kScanWStateRegs = 96;
-constexpr uint32_t kScanWIssuerRegs = 96;
-static_assert(kScanWState * kScanWStateRegs + (kScanWThreads - kScanWState) * kScanWIssuerRegs <=
-                  kScanWThreads * kScanWLaunchRegs,
-              "register split exceeds the launch allocation");
 constexpr uint32_t kStateBar = 1;         // named barrier of the state threads
 constexpr uint32_t Q_OFF_KQ = 0;          // 3 x 32 KB
 constexpr uint32_t Q_OFF_A2 = 98304;      // 2 x 24 KB: [T_b; P] hi 16 KB | T_b lo 8 KB
@@ -565,13 +557,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
-  if constexpr (kScanWStateRegs != kScanWLaunchRegs) {
-    if (!state_wg) {
-      setmaxnreg_dec<kScanWIssuerRegs>();
-    } else {
-      setmaxnreg_inc<kScanWStateRegs>();
-    }
-  }
   if (issuer) {
     // ================================ MMA / copy issuer ================================
     const uint8_t* a2_seq = a2_in + static_cast<uint64_t>(offs[n]) * HV * kUnitBytes +
@@ -991,21 +976,9 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   smaps.k = maps.k;
   smaps.q = maps.q;
   const void* vb = p.T > 0 ? static_cast<const void*>(p.v) : static_cast<const void*>(p.new_state);
-  void* ob = p.T > 0 ? static_cast<void*>(p.out) : static_cast<void*>(p.new_state);
-  if (!encode_v_map(&smaps.v, vb, Tm, p.HV) || !encode_v_map(&smaps.o, ob, Tm, p.HV)) return -2;
+  if (!encode_v_map(&smaps.v, vb, Tm, p.HV)) return -2;
   if (cudaFuncSetAttribute(scan_w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            kScanWSmem) != cudaSuccess)
-    return -1;
-  // The warpgroups' register split (setmaxnreg) must fit in what the block is launched
-  // with; a build whose launch register count came out lower is not run.
-  static int launch_regs = -1;
-  if (launch_regs < 0) {
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, scan_w_kernel) != cudaSuccess) return -1;
-    launch_regs = fa.numRegs;
-  }
-  if (static_cast<uint32_t>(launch_regs) * kScanWThreads <
-      kScanWState * kScanWStateRegs + (kScanWThreads - kScanWState) * kScanWIssuerRegs)
     return -1;
   scan_w_kernel<<<static_cast<unsigned>(p.N * p.HV), kScanWThreads, kScanWSmem, stream>>>(
       p, smaps, offs, order, a2);
