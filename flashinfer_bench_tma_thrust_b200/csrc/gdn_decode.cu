@@ -141,9 +141,10 @@ int launch_decode_t(const DecodeParams& p_in, cudaStream_t stream) {
   // Short blocks keep the end of the grid from idling SMs while the last long blocks
   // stream: measured on B200 (state GB/s by batch), four blocks per head (8 rows per
   // warp) up to 16384 heads (B = 512 at 32 v-heads) and two beyond are best, e.g. at
-  // B = 256 6.65 TB/s against 6.20 with one block per head; at small batch the split
-  // grows until the grid covers the SMs several times over.
-  int splits = heads <= 16384 ? 4 : 2;
+  // B = 256 6.65 TB/s against 6.20 with one block per head. A bf16 state (half the
+  // bytes per row) is best with one block per head (5.8 TB/s against 4.9 with four).
+  // At small batch the split grows until the grid covers the SMs several times over.
+  int splits = sizeof(S) == 4 ? (heads <= 16384 ? 4 : 2) : 1;
   const int64_t target_blocks = 148 * 4;
   while (splits < 8 && heads * splits < target_blocks) splits *= 2;
   p.splits = splits;
