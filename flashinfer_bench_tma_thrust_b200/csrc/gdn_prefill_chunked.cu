@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(128, 2)
 #pragma unroll
     for (int v = 0; v < kVT; ++v) p.new_state[sbase + v * kHeadDim] = hrow[v];
   } else if (t == 0 && p.status) {
-    atomicExch(p.status, 1);
+    atomicOr(p.status, 1);  // bit 0: a bounded wait gave up
   }
   tc_fence_before();
   __syncthreads();

@@ -91,6 +91,17 @@ __device__ long long g_prep_cycles[16];
   } while (0)
 #endif  // per (chunk, v-head): hi 16 KB + lo rows 0..63 8 KB
 
+// Status word bits (sticky, in the workspace): a bounded wait gave up; cu_seqlens held a
+// value outside [0, T] (used clamped) or ranges whose chunks overflow the workspace
+// (overlapping sequences: the call then computes nothing and passes states through).
+constexpr int kStatusWaitTimeout = 1;
+constexpr int kStatusBadSeqlens = 2;
+
+// Capacity of the workspace in (chunk) units per v-head: ceil(T / 64) + N.
+__device__ __forceinline__ int64_t unit_capacity(const PrefillParams& p) {
+  return (p.T + kC - 1) / kC + p.N;
+}
+
 __device__ __forceinline__ void seq_bounds(const PrefillParams& p, int64_t n, int64_t& start,
                                            int64_t& end) {
   start = load_index(p.cu_seqlens, p.cu_dtype, n);
@@ -115,6 +126,10 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
     const int64_t n = base + t;
     int64_t cnt = 0;
     if (n < p.N) {
+      const int64_t rs = load_index(p.cu_seqlens, p.cu_dtype, n);
+      const int64_t re = load_index(p.cu_seqlens, p.cu_dtype, n + 1);
+      if ((rs < 0 || rs > p.T || re < 0 || re > p.T) && p.status)
+        atomicOr(p.status, kStatusBadSeqlens);
       int64_t s, e;
       seq_bounds(p, n, s, e);
       cnt = e > s ? (e - s + kC - 1) / kC : 0;
@@ -143,6 +158,7 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
     if (t == 1023) carry = incl;
     __syncthreads();
   }
+  if (t == 0 && carry > unit_capacity(p) && p.status) atomicOr(p.status, kStatusBadSeqlens);
 }
 
 // ------------------------------------------------------------------ scan order
@@ -207,7 +223,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
   const int h = static_cast<int>(blockIdx.x % p.HV);
   const int64_t gchunk = blockIdx.x / p.HV;
   const int64_t total = offs[p.N];
-  if (gchunk >= total) return;
+  if (gchunk >= total || total > unit_capacity(p)) return;  // (overflow: nothing written)
   // sequence containing this chunk: the last n with offs[n] <= gchunk
   int64_t lo = 0, hi = p.N;
   while (lo < hi) {
@@ -317,7 +333,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
       PPHASE(7);  // P rows write
     }
   }
-  if (!ok && t == 0 && p.status) atomicExch(p.status, 1);
+  if (!ok && t == 0 && p.status) atomicOr(p.status, kStatusWaitTimeout);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kPrepTmemCols);
@@ -525,6 +541,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   int64_t start, end;
   seq_bounds(p, n, start, end);
 
+  const bool skip = end <= start || offs[p.N] > unit_capacity(p);
   // this thread's quarter of state row v: S[n, h, v, 32c .. 32c+32)
   const int64_t sbase = ((n * HV + h) * kHeadDim + v) * kHeadDim + 32 * ch;
   float S[32];
@@ -535,14 +552,16 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
                                : make_float4(0.f, 0.f, 0.f, 0.f);
       S[i] = x.x; S[i + 1] = x.y; S[i + 2] = x.z; S[i + 3] = x.w;
     }
-    if (end <= start) {  // empty sequence: pass the state through
+    // empty sequence, or a workspace overflow (no units were written): pass the state
+    // through
+    if (skip) {
 #pragma unroll
       for (int i = 0; i < 32; i += 4)
         *reinterpret_cast<float4*>(p.new_state + sbase + i) =
             make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
     }
   }
-  if (end <= start) return;
+  if (skip) return;
   const int64_t nch = (end - start + kC - 1) / kC;
 
   if (t == 0) {
@@ -911,7 +930,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       ok = false;
     }
   }
-  if (!ok && p.status) atomicExch(p.status, 1);
+  if (!ok && p.status) atomicOr(p.status, kStatusWaitTimeout);
   tc_fence_before();
   __syncthreads();
 #ifdef GDN_PHASE_PROFILE

@@ -116,16 +116,30 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     return ws
 
 
-def device_status(device=None) -> int:
-    """Sticky status word of the chunked kernel on `device` (0 = every bounded wait
-    completed; 1 = a wait gave up and its outputs are invalid). Synchronises."""
+def _device_key(device):
     device = torch.device(device or torch.cuda.current_device())
     if device.type == "cuda" and device.index is None:
         device = torch.device("cuda", torch.cuda.current_device())
-    ws = _workspaces.get((device.type, device.index))
+    return (device.type, device.index)
+
+
+def device_status(device=None) -> int:
+    """Sticky status word of the chunked kernel on `device`, a bit set: 0 = clean;
+    bit 0 (1) = a bounded wait gave up (outputs of that call invalid); bit 1 (2) =
+    cu_seqlens held a value outside [0, T] (used clamped) or overlapping ranges whose
+    chunks overflow the workspace (that call computed nothing and passed states
+    through). Synchronises."""
+    ws = _workspaces.get(_device_key(device))
     if ws is None:
         return 0
     return int(ws[:4].view(torch.int32).item())
+
+
+def reset_device_status(device=None) -> None:
+    """Clear the sticky status word on `device` (stream-ordered on the current stream)."""
+    ws = _workspaces.get(_device_key(device))
+    if ws is not None:
+        ws[:4].zero_()
 
 
 def _aligned(t):

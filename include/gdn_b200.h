@@ -159,9 +159,13 @@ GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* 
  *                    operand image and the chunk's gates — then the state scan);
  *                    with less, but at least 256 bytes, it runs the fused
  *                    single-kernel path. The first 4 bytes are a sticky status
- *                    word that a kernel sets to 1 if one of its bounded waits gave
- *                    up (read it with gdn_prefill_chunked_status). Calls that
- *                    share a workspace must be stream-ordered.
+ *                    word, a bit set (read it with gdn_prefill_chunked_status):
+ *                    bit 0 = one of a kernel's bounded waits gave up (that call's
+ *                    outputs are invalid); bit 1 = cu_seqlens held a value outside
+ *                    [0, T] (used clamped) or overlapping ranges whose chunks
+ *                    overflow the two-phase workspace (that call computed nothing
+ *                    and passed the states through). Calls that share a workspace
+ *                    must be stream-ordered.
  *
  * q, k, v and out must be 16-byte aligned (q/k are read by TMA); T < 2^31.
  * Stream-ordered launches, no host synchronisation (two-phase path: chunk offsets,
@@ -179,7 +183,8 @@ GDN_API int gdn_prefill_chunked_fwd(const void* q, const void* k, const void* v,
                                     int32_t HV, int32_t D, void* workspace,
                                     size_t workspace_bytes, void* stream);
 
-/* Copy the workspace status word to *host_status (synchronises `stream`). */
+/* Copy the workspace status word (the bit set above) to *host_status (synchronises
+ * `stream`). Clearing it is the caller's: it is the workspace's first 4 bytes. */
 GDN_API int gdn_prefill_chunked_status(const void* workspace, int* host_status, void* stream);
 
 /*

@@ -121,3 +121,32 @@ def test_partitioned_prefill_reassembles_to_full_call():
     out, state = PT.assemble_prefill(parts, x.q.shape[0], 3, 32, x.cu_seqlens)
     assert_out_close(out, ref_out, "partitioned vs full")
     assert_state_close(state, ref_state, PREFILL_STATE_ATOL, "partitioned vs full")
+
+
+def test_chunked_flags_bad_cu_seqlens_without_faulting():
+    """cu_seqlens outside [0, T] is used clamped and flagged (status bit 1); overlapping
+    ranges whose chunks would overflow the two-phase workspace are flagged and compute
+    nothing (states passed through) — no access leaves the workspace or the tensors."""
+    x = to_dev(W.prefill_inputs([640], HQ=2, HV=4, seed=5))
+    prefill.reset_device_status()
+    args = list(x.args())
+    # overlap: sequences [0, 640), (640 -> 0: empty), [0, 640): 20 chunks > 10 + 3 capacity
+    args[8] = torch.tensor([0, 640, 0, 640], dtype=torch.int32, device="cuda")
+    state = torch.randn(3, 4, 128, 128, device="cuda")
+    args[3] = state
+    out, ns = prefill.kernel(*args)
+    torch.cuda.synchronize()
+    assert prefill.device_status() & 2
+    assert torch.equal(ns, state)
+    prefill.reset_device_status()
+    # out of range: [0, 700) with T = 640 is clamped to [0, 640)
+    args[8] = torch.tensor([0, 700], dtype=torch.int64, device="cuda")
+    args[3] = x.state
+    out, ns = prefill.kernel(*args)
+    ref_out, ref_ns = prefill.kernel(*x.args())
+    torch.cuda.synchronize()
+    assert prefill.device_status() & 2
+    assert torch.equal(out, ref_out) and torch.equal(ns, ref_ns)
+    prefill.reset_device_status()
+    prefill.kernel(*x.args())
+    assert prefill.device_status() == 0
