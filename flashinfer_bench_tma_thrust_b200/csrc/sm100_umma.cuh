@@ -344,7 +344,12 @@ __device__ __forceinline__ uint32_t pack2_rn(float x0, float x1) {
 __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
   hi = pack2_rn(x0, x1);
   const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xffff0000u);
-  lo = pack2_rn(x0 - h0, x1 - h1);
+  float r0, r1;  // both residuals with one packed subtraction
+  asm("{\n\t.reg .b64 a, b, c;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "sub.rn.f32x2 c, a, b;\n\tmov.b64 {%0, %1}, c;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(x0), "f"(x1), "f"(h0), "f"(h1));
+  lo = pack2_rn(r0, r1);
 }
 
 }  // namespace sm100
