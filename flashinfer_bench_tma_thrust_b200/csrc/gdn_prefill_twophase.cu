@@ -752,7 +752,8 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
 #pragma unroll
       for (int w = 0; w < 16; ++w) {
         uint32_t hw, lw;
-        split2(scale * S[2 * w], scale * S[2 * w + 1], hw, lw);
+        const float2 gs = mul2(make_float2(scale, scale), make_float2(S[2 * w], S[2 * w + 1]));
+        split2(gs.x, gs.y, hw, lw);
         hl[w] = __uint_as_float(hw);
         hl[16 + w] = __uint_as_float(lw);
       }
@@ -834,7 +835,12 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         tmem_ld32(lane + TP_S + 32 * ch, d0);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) S[i] = fmaf(g_prev, S[i], d0[i]);
+        for (int i = 0; i < 32; i += 2) {
+          const float2 r = fma2(make_float2(g_prev, g_prev), make_float2(S[i], S[i + 1]),
+                                make_float2(d0[i], d0[i + 1]));
+          S[i] = r.x;
+          S[i + 1] = r.y;
+        }
       }
       g_prev = sGam[kC - 1];
       SEVENT(4);
@@ -886,7 +892,12 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         tmem_ld16(lane + TP_GO + 16 * ch, u);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) u[i] *= sF[16 * ch + i];
+        for (int i = 0; i < 16; i += 2) {
+          const float2 r = mul2(make_float2(u[i], u[i + 1]),
+                                *reinterpret_cast<const float2*>(sF + 16 * ch + i));
+          u[i] = r.x;
+          u[i + 1] = r.y;
+        }
         uint32_t hw[8], lw[8];
         split_words<8>(u, hw, lw);
         tmem_st8(lane + d1c + 16 * ch, hw);
@@ -900,8 +911,11 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int i0 = 16 * ch + 2 * i;
-          opk[i] = pack2_rn(p.scale * fmaf(sGam[i0], qv[2 * i], o[2 * i]),
-                            p.scale * fmaf(sGam[i0 + 1], qv[2 * i + 1], o[2 * i + 1]));
+          const float2 r = mul2(make_float2(p.scale, p.scale),
+                                fma2(*reinterpret_cast<const float2*>(sGam + i0),
+                                     make_float2(qv[2 * i], qv[2 * i + 1]),
+                                     make_float2(o[2 * i], o[2 * i + 1])));
+          opk[i] = pack2_rn(r.x, r.y);
         }
         o_cs = cs;
         o_L = L;
