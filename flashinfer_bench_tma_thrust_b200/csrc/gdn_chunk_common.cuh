@@ -411,61 +411,91 @@ __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float
   }
   __syncthreads();
   // Two levels, every warp busy at each (T_IJ = -T_II A_IJ T_JJ for the lower blocks
-  // of a block-diagonal inverse):
-  // level 1, 16 -> 32: blocks (1,0) [warps 0-3] and (3,2) [warps 4-7]; 2 outputs per
-  // thread (row r, columns c0, c0+1); scratch W in block (0, 2 + g).
+  // of a block-diagonal inverse). Lanes own columns: the left operand of a k-quad comes
+  // as one broadcast float4 per row, the right operand as one conflict-free 32-bit load
+  // per lane (a float4 per lane over eight addresses would cost four shared-memory
+  // wavefronts for four products).
+  // level 1, 16 -> 32: blocks (1,0) [warps 0-3] and (3,2) [warps 4-7]; rows r0, r0 + 1
+  // and column c per thread; scratch W in block (0, 2 + g).
   {
-    const int g = warp >> 2, q = t & 127, r = q >> 3, c0 = (q & 7) * 2;
+    const int g = warp >> 2, r0 = 4 * (warp & 3) + 2 * (lane >> 4), c = lane & 15;
     const int I = 2 * g + 1, J = 2 * g;
     float w0 = 0.f, w1 = 0.f;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float a = sAf[Lay::idx(16 * I + r, 16 * J + k)];
-      const float2 tv = *reinterpret_cast<const float2*>(sTf + Lay::idx(16 * J + k, 16 * J + c0));
-      w0 = fmaf(a, tv.x, w0);
-      w1 = fmaf(a, tv.y, w1);
+    for (int k = 0; k < 16; k += 4) {
+      const float4 a0 = *reinterpret_cast<const float4*>(sAf + Lay::idx(16 * I + r0, 16 * J + k));
+      const float4 a1 =
+          *reinterpret_cast<const float4*>(sAf + Lay::idx(16 * I + r0 + 1, 16 * J + k));
+      const float t0 = sTf[Lay::idx(16 * J + k, 16 * J + c)];
+      const float t1 = sTf[Lay::idx(16 * J + k + 1, 16 * J + c)];
+      const float t2 = sTf[Lay::idx(16 * J + k + 2, 16 * J + c)];
+      const float t3 = sTf[Lay::idx(16 * J + k + 3, 16 * J + c)];
+      w0 = fmaf(a0.x, t0, w0); w0 = fmaf(a0.y, t1, w0);
+      w0 = fmaf(a0.z, t2, w0); w0 = fmaf(a0.w, t3, w0);
+      w1 = fmaf(a1.x, t0, w1); w1 = fmaf(a1.y, t1, w1);
+      w1 = fmaf(a1.z, t2, w1); w1 = fmaf(a1.w, t3, w1);
     }
-    *reinterpret_cast<float2*>(sTf + Lay::idx(r, 32 + 16 * g + c0)) = make_float2(w0, w1);
+    sTf[Lay::idx(r0, 32 + 16 * g + c)] = w0;
+    sTf[Lay::idx(r0 + 1, 32 + 16 * g + c)] = w1;
     named_bar_sync(2 + g, 128);
-    // T_II is lower triangular: rows r of this warp need k <= r only
+    // T_II is lower triangular: rows of this warp need k < 4 (warp % 4) + 4 only
     const int kmax = 4 * (warp & 3) + 4;
     float v0 = 0.f, v1 = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < kmax; ++k) {
-      const float a = sTf[Lay::idx(16 * I + r, 16 * I + k)];
-      const float2 wv = *reinterpret_cast<const float2*>(sTf + Lay::idx(k, 32 + 16 * g + c0));
-      v0 = fmaf(a, wv.x, v0);
-      v1 = fmaf(a, wv.y, v1);
+#pragma unroll 1
+    for (int k = 0; k < kmax; k += 4) {
+      const float4 a0 = *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * I + r0, 16 * I + k));
+      const float4 a1 =
+          *reinterpret_cast<const float4*>(sTf + Lay::idx(16 * I + r0 + 1, 16 * I + k));
+      const float t0 = sTf[Lay::idx(k, 32 + 16 * g + c)];
+      const float t1 = sTf[Lay::idx(k + 1, 32 + 16 * g + c)];
+      const float t2 = sTf[Lay::idx(k + 2, 32 + 16 * g + c)];
+      const float t3 = sTf[Lay::idx(k + 3, 32 + 16 * g + c)];
+      v0 = fmaf(a0.x, t0, v0); v0 = fmaf(a0.y, t1, v0);
+      v0 = fmaf(a0.z, t2, v0); v0 = fmaf(a0.w, t3, v0);
+      v1 = fmaf(a1.x, t0, v1); v1 = fmaf(a1.y, t1, v1);
+      v1 = fmaf(a1.z, t2, v1); v1 = fmaf(a1.w, t3, v1);
     }
-    *reinterpret_cast<float2*>(sTf + Lay::idx(16 * I + r, 16 * J + c0)) = make_float2(-v0, -v1);
+    sTf[Lay::idx(16 * I + r0, 16 * J + c)] = -v0;
+    sTf[Lay::idx(16 * I + r0 + 1, 16 * J + c)] = -v1;
   }
   __syncthreads();
-  // level 2, 32 -> 64: block rows 32..63 x cols 0..31, 4 outputs per thread; scratch W
-  // in rows 0..31 x cols 32..63 (the level-1 scratch is consumed)
+  // level 2, 32 -> 64: block rows 32..63 x cols 0..31; warp w owns rows 4w..4w+3 and
+  // lane = column; scratch W in rows 0..31 x cols 32..63 (the level-1 scratch is consumed)
   {
-    const int r = t >> 3, c0 = (t & 7) * 4;
+    const int r0 = 4 * warp, c = lane;
     float w[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      const float a = sAf[Lay::idx(32 + r, k)];
-      const float4 tv = *reinterpret_cast<const float4*>(sTf + Lay::idx(k, c0));
-      w[0] = fmaf(a, tv.x, w[0]); w[1] = fmaf(a, tv.y, w[1]);
-      w[2] = fmaf(a, tv.z, w[2]); w[3] = fmaf(a, tv.w, w[3]);
+#pragma unroll 2
+    for (int k = 0; k < 32; k += 4) {
+      float tv[4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) tv[kk] = sTf[Lay::idx(k + kk, c)];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 a = *reinterpret_cast<const float4*>(sAf + Lay::idx(32 + r0 + i, k));
+        w[i] = fmaf(a.x, tv[0], w[i]); w[i] = fmaf(a.y, tv[1], w[i]);
+        w[i] = fmaf(a.z, tv[2], w[i]); w[i] = fmaf(a.w, tv[3], w[i]);
+      }
     }
-    *reinterpret_cast<float4*>(sTf + Lay::idx(r, 32 + c0)) = make_float4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sTf[Lay::idx(r0 + i, 32 + c)] = w[i];
     __syncthreads();
-    // T_{[32,64)} is lower triangular: rows of warp w (4w .. 4w+3) need k < 4w + 4
-    const int kmax = 4 * warp + 4;
+    // T_{[32,64)} is lower triangular: rows of warp w need k < 4w + 4
+    const int kmax = r0 + 4;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-    for (int k = 0; k < kmax; ++k) {
-      const float a = sTf[Lay::idx(32 + r, 32 + k)];
-      const float4 wv = *reinterpret_cast<const float4*>(sTf + Lay::idx(k, 32 + c0));
-      v[0] = fmaf(a, wv.x, v[0]); v[1] = fmaf(a, wv.y, v[1]);
-      v[2] = fmaf(a, wv.z, v[2]); v[3] = fmaf(a, wv.w, v[3]);
+#pragma unroll 1
+    for (int k = 0; k < kmax; k += 4) {
+      float wv[4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) wv[kk] = sTf[Lay::idx(k + kk, 32 + c)];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 a = *reinterpret_cast<const float4*>(sTf + Lay::idx(32 + r0 + i, 32 + k));
+        v[i] = fmaf(a.x, wv[0], v[i]); v[i] = fmaf(a.y, wv[1], v[i]);
+        v[i] = fmaf(a.z, wv[2], v[i]); v[i] = fmaf(a.w, wv[3], v[i]);
+      }
     }
-    *reinterpret_cast<float4*>(sTf + Lay::idx(32 + r, c0)) =
-        make_float4(-v[0], -v[1], -v[2], -v[3]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sTf[Lay::idx(32 + r0 + i, c)] = -v[i];
   }
   __syncthreads();
   {
