@@ -391,19 +391,27 @@ template <class Lay>
 __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float* sBeta,
                                              uint8_t* tb_hi, uint8_t* tb_lo) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  if (warp < 4 && lane < 16) {
-    // column `lane` of the inverse of the unit lower block b0: x_i = d_i - sum_{j<i} A_ij x_j
-    const int b0 = warp * 16;
+  if (warp < 2) {
+    // column `lane % 16` of the inverse of the unit lower block b0 (each half-warp one
+    // block): x_i = d_i - sum_{j<i} A_ij x_j, right-looking two columns per step so
+    // that A_{i,j}, A_{i,j+1} come as one broadcast 64-bit load (same order of updates
+    // per x_i as one column per step)
+    const int b0 = (2 * warp + (lane >> 4)) * 16, l = lane & 15;
     float x[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = (i == lane) ? 1.f : 0.f;
+    for (int i = 0; i < 16; ++i) x[i] = (i == l) ? 1.f : 0.f;
 #pragma unroll
-    for (int j = 0; j < 15; ++j) {
+    for (int j = 0; j < 16; j += 2) {
+      x[j + 1] = fmaf(-sAf[Lay::idx(b0 + j + 1, b0 + j)], x[j], x[j + 1]);
 #pragma unroll
-      for (int i = j + 1; i < 16; ++i) x[i] = fmaf(-sAf[Lay::idx(b0 + i, b0 + j)], x[j], x[i]);
+      for (int i = j + 2; i < 16; ++i) {
+        const float2 a = *reinterpret_cast<const float2*>(sAf + Lay::idx(b0 + i, b0 + j));
+        x[i] = fmaf(-a.x, x[j], x[i]);
+        x[i] = fmaf(-a.y, x[j + 1], x[i]);
+      }
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) sTf[Lay::idx(b0 + i, b0 + lane)] = x[i];
+    for (int i = 0; i < 16; ++i) sTf[Lay::idx(b0 + i, b0 + l)] = x[i];
   } else if (warp >= 4 && warp < 6) {
     // block (0, 1) of T must read as zero in the level-2 product below
     const int q = t - 128, row = q >> 2, col = 16 + (q & 3) * 4;

@@ -300,17 +300,12 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
         mma_commit_w(bar_mma);
       }
       // meanwhile: the T_b rows of [T_b; P] are the T_b tiles themselves (same swizzled
-      // row image): copy hi to rows 0..63 of the hi part, lo to the lo part
+      // row image): bulk-copy hi to rows 0..63 of the hi part, lo to the lo part
       uint8_t* dst = a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) * kUnitBytes;
-      {
-        const uint4* src_hi = reinterpret_cast<const uint4*>(sm + P_OFF_TB_HI);
-        const uint4* src_lo = reinterpret_cast<const uint4*>(sm + P_OFF_TB_LO);
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int idx = t + q * kPrepThreads;  // 512 x 16 B = 8 KB per tile
-          reinterpret_cast<uint4*>(dst)[idx] = src_hi[idx];
-          reinterpret_cast<uint4*>(dst + 16384)[idx] = src_lo[idx];
-        }
+      if (t == 32) {
+        bulk_store(dst, sm + P_OFF_TB_HI, 8192);
+        bulk_store(dst + 16384, sm + P_OFF_TB_LO, 8192);
+        bulk_commit();
       }
       PPHASE(5);  // P issue + T_b copy
       ok = mbar_wait(bar_mma, 1);
@@ -333,6 +328,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
       PPHASE(7);  // P rows write
     }
   }
+  if (t == 32) bulk_wait_all();  // the T_b tiles stay in place until copied
   if (!ok && t == 0 && p.status) atomicOr(p.status, kStatusWaitTimeout);
   tc_fence_before();
   __syncthreads();

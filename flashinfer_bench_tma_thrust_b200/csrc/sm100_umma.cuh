@@ -371,5 +371,20 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
   return r;
 }
 
+// Bulk copy shared -> global through the async proxy (no multicast), tracked by the
+// issuing thread's bulk groups.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+               "r"(smem_u32(ssrc)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// every committed bulk store of this thread has completed (writes performed)
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 }  // namespace sm100
 }  // namespace gdn
