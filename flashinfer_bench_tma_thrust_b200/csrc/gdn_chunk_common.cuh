@@ -428,23 +428,25 @@ __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float
   {
     const int g = warp >> 2, r0 = 4 * (warp & 3) + 2 * (lane >> 4), c = lane & 15;
     const int I = 2 * g + 1, J = 2 * g;
-    float w0 = 0.f, w1 = 0.f;
+    {
+      // W = A_IJ T_JJ with warps over column quads (row = lane % 16, two columns per
+      // lane): T_JJ is lower triangular, so the warp's k loop starts at its first column
+      const int cq = 4 * (warp & 3), cw = cq + 2 * (lane >> 4), rw = lane & 15;
+      float w0 = 0.f, w1 = 0.f;
+#pragma unroll 1
+      for (int k = cq; k < 16; k += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(sAf + Lay::idx(16 * I + rw, 16 * J + k));
+        float2 tv[4];
 #pragma unroll
-    for (int k = 0; k < 16; k += 4) {
-      const float4 a0 = *reinterpret_cast<const float4*>(sAf + Lay::idx(16 * I + r0, 16 * J + k));
-      const float4 a1 =
-          *reinterpret_cast<const float4*>(sAf + Lay::idx(16 * I + r0 + 1, 16 * J + k));
-      const float t0 = sTf[Lay::idx(16 * J + k, 16 * J + c)];
-      const float t1 = sTf[Lay::idx(16 * J + k + 1, 16 * J + c)];
-      const float t2 = sTf[Lay::idx(16 * J + k + 2, 16 * J + c)];
-      const float t3 = sTf[Lay::idx(16 * J + k + 3, 16 * J + c)];
-      w0 = fmaf(a0.x, t0, w0); w0 = fmaf(a0.y, t1, w0);
-      w0 = fmaf(a0.z, t2, w0); w0 = fmaf(a0.w, t3, w0);
-      w1 = fmaf(a1.x, t0, w1); w1 = fmaf(a1.y, t1, w1);
-      w1 = fmaf(a1.z, t2, w1); w1 = fmaf(a1.w, t3, w1);
+        for (int kk = 0; kk < 4; ++kk)
+          tv[kk] = *reinterpret_cast<const float2*>(sTf + Lay::idx(16 * J + k + kk, 16 * J + cw));
+        w0 = fmaf(a.x, tv[0].x, w0); w0 = fmaf(a.y, tv[1].x, w0);
+        w0 = fmaf(a.z, tv[2].x, w0); w0 = fmaf(a.w, tv[3].x, w0);
+        w1 = fmaf(a.x, tv[0].y, w1); w1 = fmaf(a.y, tv[1].y, w1);
+        w1 = fmaf(a.z, tv[2].y, w1); w1 = fmaf(a.w, tv[3].y, w1);
+      }
+      *reinterpret_cast<float2*>(sTf + Lay::idx(rw, 32 + 16 * g + cw)) = make_float2(w0, w1);
     }
-    sTf[Lay::idx(r0, 32 + 16 * g + c)] = w0;
-    sTf[Lay::idx(r0 + 1, 32 + 16 * g + c)] = w1;
     named_bar_sync(2 + g, 128);
     // T_II is lower triangular: rows of this warp need k < 4 (warp % 4) + 4 only
     const int kmax = 4 * (warp & 3) + 4;
@@ -471,21 +473,30 @@ __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float
   // lane = column; scratch W in rows 0..31 x cols 32..63 (the level-1 scratch is consumed)
   {
     const int r0 = 4 * warp, c = lane;
-    float w[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-    for (int k = 0; k < 32; k += 4) {
-      float tv[4];
+    {
+      // W = A_21 T_11 with warp w over columns 4w..4w+3 and lane = row: T_11 is lower
+      // triangular, so the warp's k loop starts at 4w
+      const int cq = 4 * warp;
+      float w[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int k = cq; k < 32; k += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(sAf + Lay::idx(32 + lane, k));
+        float4 tv[4];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) tv[kk] = sTf[Lay::idx(k + kk, c)];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 a = *reinterpret_cast<const float4*>(sAf + Lay::idx(32 + r0 + i, k));
-        w[i] = fmaf(a.x, tv[0], w[i]); w[i] = fmaf(a.y, tv[1], w[i]);
-        w[i] = fmaf(a.z, tv[2], w[i]); w[i] = fmaf(a.w, tv[3], w[i]);
+        for (int kk = 0; kk < 4; ++kk)
+          tv[kk] = *reinterpret_cast<const float4*>(sTf + Lay::idx(k + kk, cq));
+        w[0] = fmaf(a.x, tv[0].x, w[0]); w[0] = fmaf(a.y, tv[1].x, w[0]);
+        w[0] = fmaf(a.z, tv[2].x, w[0]); w[0] = fmaf(a.w, tv[3].x, w[0]);
+        w[1] = fmaf(a.x, tv[0].y, w[1]); w[1] = fmaf(a.y, tv[1].y, w[1]);
+        w[1] = fmaf(a.z, tv[2].y, w[1]); w[1] = fmaf(a.w, tv[3].y, w[1]);
+        w[2] = fmaf(a.x, tv[0].z, w[2]); w[2] = fmaf(a.y, tv[1].z, w[2]);
+        w[2] = fmaf(a.z, tv[2].z, w[2]); w[2] = fmaf(a.w, tv[3].z, w[2]);
+        w[3] = fmaf(a.x, tv[0].w, w[3]); w[3] = fmaf(a.y, tv[1].w, w[3]);
+        w[3] = fmaf(a.z, tv[2].w, w[3]); w[3] = fmaf(a.w, tv[3].w, w[3]);
       }
+      *reinterpret_cast<float4*>(sTf + Lay::idx(lane, 32 + cq)) =
+          make_float4(w[0], w[1], w[2], w[3]);
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sTf[Lay::idx(r0 + i, 32 + c)] = w[i];
     __syncthreads();
     // T_{[32,64)} is lower triangular: rows of warp w need k < 4w + 4
     const int kmax = r0 + 4;
