@@ -354,10 +354,11 @@ __device__ __forceinline__ void build_a_m_256(uint32_t ts_row, float* sAf, const
       float4 w;
       const int jj = c0 + j;
       const float4 g = *reinterpret_cast<const float4*>(sG + jj);
-      w.x = (jj + 0 < r) ? bi * ex2(gi - g.x) * srow[j + 0] : 0.f;
-      w.y = (jj + 1 < r) ? bi * ex2(gi - g.y) * srow[j + 1] : 0.f;
-      w.z = (jj + 2 < r) ? bi * ex2(gi - g.z) * srow[j + 2] : 0.f;
-      w.w = (jj + 3 < r) ? bi * ex2(gi - g.w) * srow[j + 3] : 0.f;
+      // unmasked: the solve reads only the strict lower triangle of A
+      w.x = bi * ex2(gi - g.x) * srow[j + 0];
+      w.y = bi * ex2(gi - g.y) * srow[j + 1];
+      w.z = bi * ex2(gi - g.z) * srow[j + 2];
+      w.w = bi * ex2(gi - g.w) * srow[j + 3];
       *reinterpret_cast<float4*>(sAf + Lay::idx(r, jj)) = w;
     }
   } else {
@@ -530,8 +531,7 @@ __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int m = nn + e;
-        const bool lower = (m >> 4) < (j >> 4) || ((m >> 4) == (j >> 4) && m <= j);
-        vals[c + e] = lower ? tvs[e] : 0.f;
+        vals[c + e] = m <= j ? tvs[e] : 0.f;  // T's upper triangle holds scratch
       }
     }
 #pragma unroll
