@@ -344,10 +344,14 @@ template <class Lay>
 __device__ __forceinline__ void build_a_m_256(uint32_t ts_row, float* sAf, const float* sG,
                                               const float* sBeta, uint8_t* m_hi, uint8_t* m_lo) {
   const int t = threadIdx.x, r = t & 127, c0 = (t >> 7) * 32;
-  float srow[32];
-  tmem_ld32(ts_row, srow);
-  tmem_ld_wait();
+  // where this warp's 32 x 32 quarter lies against the diagonal (warp-uniform): its
+  // row block rb and column block cb within A or M
+  const int rb = (r & 63) >> 5, cb = t >> 7;
   if (r < kC) {
+    if (cb > rb) return;  // above the diagonal: the solve reads only A's strict lower part
+    float srow[32];
+    tmem_ld32(ts_row, srow);
+    tmem_ld_wait();
     const float gi = sG[r], bi = sBeta[r];
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
@@ -363,14 +367,38 @@ __device__ __forceinline__ void build_a_m_256(uint32_t ts_row, float* sAf, const
     }
   } else {
     const int i = r - kC;
-    const float gi = sG[i];
+    if (cb > rb) {  // above the diagonal: M is zero there
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const float4 g = *reinterpret_cast<const float4*>(sG + c0 + j);
-      srow[j] = (c0 + j <= i) ? ex2(gi - g.x) * srow[j] : 0.f;
-      srow[j + 1] = (c0 + j + 1 <= i) ? ex2(gi - g.y) * srow[j + 1] : 0.f;
-      srow[j + 2] = (c0 + j + 2 <= i) ? ex2(gi - g.z) * srow[j + 2] : 0.f;
-      srow[j + 3] = (c0 + j + 3 <= i) ? ex2(gi - g.w) * srow[j + 3] : 0.f;
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t off = sw128_chunk(i, (c0 >> 3) + c);
+        *reinterpret_cast<uint4*>(m_hi + off) = z;
+        *reinterpret_cast<uint4*>(m_lo + off) = z;
+      }
+      return;
+    }
+    float srow[32];
+    tmem_ld32(ts_row, srow);
+    tmem_ld_wait();
+    const float gi = sG[i];
+    if (cb < rb) {  // below the diagonal: no mask
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 g = *reinterpret_cast<const float4*>(sG + c0 + j);
+        srow[j] = ex2(gi - g.x) * srow[j];
+        srow[j + 1] = ex2(gi - g.y) * srow[j + 1];
+        srow[j + 2] = ex2(gi - g.z) * srow[j + 2];
+        srow[j + 3] = ex2(gi - g.w) * srow[j + 3];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 g = *reinterpret_cast<const float4*>(sG + c0 + j);
+        srow[j] = (c0 + j <= i) ? ex2(gi - g.x) * srow[j] : 0.f;
+        srow[j + 1] = (c0 + j + 1 <= i) ? ex2(gi - g.y) * srow[j + 1] : 0.f;
+        srow[j + 2] = (c0 + j + 2 <= i) ? ex2(gi - g.z) * srow[j + 2] : 0.f;
+        srow[j + 3] = (c0 + j + 3 <= i) ? ex2(gi - g.w) * srow[j + 3] : 0.f;
+      }
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -519,29 +547,46 @@ __device__ __forceinline__ void solve_tb_256(float* sAf, float* sTf, const float
   }
   __syncthreads();
   {
-    // T_b = T diag(beta), MN-major rows j x cols n: a quarter row (2 chunks) per thread
-    const int j = t & (kC - 1), qq = t >> 6;
-    float vals[16];
+    // T_b = T diag(beta), MN-major rows j x cols n: a quarter row (2 chunks) per thread.
+    // Warp-uniform cases: the warp's 16 columns lie right of all its 32 rows (zero),
+    // left of all of them (no mask), or across the diagonal (masked: T's upper triangle
+    // holds scratch).
+    const int j = t & (kC - 1), qq = t >> 6, jb = (t >> 5) & 1;
+    if (16 * qq > 32 * jb + 31) {
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-    for (int c = 0; c < 16; c += 4) {
-      const int nn = qq * 16 + c;
-      const float4 tv = *reinterpret_cast<const float4*>(sTf + Lay::idx(j, nn));
-      const float4 bv = *reinterpret_cast<const float4*>(sBeta + nn);
-      const float tvs[4] = {tv.x * bv.x, tv.y * bv.y, tv.z * bv.z, tv.w * bv.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int m = nn + e;
-        vals[c + e] = m <= j ? tvs[e] : 0.f;  // T's upper triangle holds scratch
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t off = sw128_chunk(j, qq * 2 + c);
+        *reinterpret_cast<uint4*>(tb_hi + off) = z;
+        *reinterpret_cast<uint4*>(tb_lo + off) = z;
       }
-    }
+    } else {
+      const bool full = 16 * qq + 15 <= 32 * jb;
+      float vals[16];
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      uint32_t hw[4], lw[4];
+      for (int c = 0; c < 16; c += 4) {
+        const int nn = qq * 16 + c;
+        const float4 tv = *reinterpret_cast<const float4*>(sTf + Lay::idx(j, nn));
+        const float4 bv = *reinterpret_cast<const float4*>(sBeta + nn);
+        vals[c] = tv.x * bv.x;
+        vals[c + 1] = tv.y * bv.y;
+        vals[c + 2] = tv.z * bv.z;
+        vals[c + 3] = tv.w * bv.w;
+      }
+      if (!full) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) split2(vals[c * 8 + 2 * e], vals[c * 8 + 2 * e + 1], hw[e], lw[e]);
-      const uint32_t off = sw128_chunk(j, qq * 2 + c);
-      *reinterpret_cast<uint4*>(tb_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(tb_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        for (int c = 0; c < 16; ++c)
+          if (qq * 16 + c > j) vals[c] = 0.f;
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) split2(vals[c * 8 + 2 * e], vals[c * 8 + 2 * e + 1], hw[e], lw[e]);
+        const uint32_t off = sw128_chunk(j, qq * 2 + c);
+        *reinterpret_cast<uint4*>(tb_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(tb_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
     }
   }
 }
