@@ -487,7 +487,7 @@ constexpr uint32_t Q_OFF_A2 = 98304;      // 2 x 24 KB: [T_b; P] hi 16 KB | T_b 
 constexpr uint32_t Q_OFF_V = 147456;      // 2 x 16 KB: V tile, rows j x 128 v
 constexpr uint32_t Q_OFF_B = 180224;      // B_c^T image: hi 16 KB (128 rows) | lo 8 KB (K rows)
 constexpr uint32_t Q_OFF_GATES = 204800;  // 2 x (gamma_j, f_j): 2 x 512 B, from the prep
-constexpr uint32_t Q_OFF_BAR = 206848;    // 14 mbarriers, TMEM slot
+constexpr uint32_t Q_OFF_BAR = 206848;    // 15 mbarriers, TMEM slot
 #ifdef GDN_PHASE_PROFILE
 constexpr uint32_t Q_OFF_PROF = 206848 + 256;  // debug phase timers (16 x 8 B)
 #endif
@@ -520,6 +520,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   uint64_t* bar_op = bar_kq + 11;   //              S operand stored
   uint64_t* bar_u = bar_kq + 12;    //              U'^T stored
   uint64_t* bar_bi = bar_kq + 13;   //              B_c image stored
+  uint64_t* bar_o = bar_kq + 14;    //              chunk's output rows read
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Q_OFF_BAR + 128);
 #ifdef GDN_PHASE_PROFILE
   long long* sprof_ = reinterpret_cast<long long*>(sm + Q_OFF_PROF);
@@ -562,7 +563,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
 
   if (t == 0) {
     for (int i = 0; i < 10; ++i) mbar_init(&bar_kq[i], 1);
-    for (int i = 10; i < 14; ++i) mbar_init(&bar_kq[i], kScanWState / 32);
+    for (int i = 10; i < 15; ++i) mbar_init(&bar_kq[i], kScanWState / 32);
     fence_mbar_init();
   }
   if (issuer) tmem_alloc(tmem_slot, kScanTTmemCols);
@@ -723,9 +724,16 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       // B_{c+1} for chunk c+1's state-side work (D1_c's buffer is read: U'_c is stored)
       IPHASE(6);  // G1', G1a wait, G3
       SEVENT(22);
-      if (c + 2 < nch && !issue_b(c + 1)) {
-        ok = false;
-        break;
+      // B_{c+1} overwrites the (QH)^T half of D1_c: after the state warps have read
+      // chunk c's output rows
+      if (c + 2 < nch) {
+        ok = mbar_wait_spin(bar_o, static_cast<uint32_t>(c & 1)) && ok;
+        tc_fence_after();
+        __syncwarp();
+        if (!ok || !issue_b(c + 1)) {
+          ok = false;
+          break;
+        }
       }
       IPHASE(7);  // B issue
       SEVENT(23);
@@ -898,27 +906,33 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         split_words<8>(u, hw, lw);
         tmem_st8(lane + d1c + 16 * ch, hw);
         tmem_st8(lane + d1c + 16 * ch + 8, lw);
-        // O^T row v, tokens i in [16c, 16c+16): scale (gamma_i (QH)^T + (PX)^T); read before
-        // U' is signalled (B_{c+1} then overwrites the (QH)^T half)
+        tmem_st_wait();
+      }
+      signal(bar_u);
+      SEVENT(10);
+      {
+        // O^T row v, tokens i in [16c, 16c+16): scale (gamma_i (QH)^T + (PX)^T), read
+        // before B_{c+1} overwrites the (QH)^T half (the issuer waits for bar_o)
         float o[16], qv[16];
         tmem_ld16(lane + TP_GO + 64 + 16 * ch, o);
         tmem_ld16(lane + d1c + 64 + 16 * ch, qv);
+        // the gates too: after bar_o the issuer may refill this gate buffer
+        float2 gm[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) gm[i] = *reinterpret_cast<const float2*>(sGam + 16 * ch + 2 * i);
         tmem_ld_wait();
+        signal(bar_o);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int i0 = 16 * ch + 2 * i;
           const float2 r = mul2(make_float2(p.scale, p.scale),
-                                fma2(*reinterpret_cast<const float2*>(sGam + i0),
+                                fma2(gm[i],
                                      make_float2(qv[2 * i], qv[2 * i + 1]),
                                      make_float2(o[2 * i], o[2 * i + 1])));
           opk[i] = pack2_rn(r.x, r.y);
         }
         o_cs = cs;
         o_L = L;
-        tmem_st_wait();
       }
-      signal(bar_u);
-      SEVENT(10);
       store_output();
       SEVENT(3);
       SPHASE(6);  // U' and output rows
