@@ -161,6 +161,30 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
   if (t == 0 && carry > unit_capacity(p) && p.status) atomicOr(p.status, kStatusBadSeqlens);
 }
 
+// ------------------------------------------------------------------ chunk table
+// table[g] = cs * 128 + L for every chunk g < offs[N]: its first token cs and its length
+// L (1..64), so that each prep block finds its chunk with one load instead of a binary
+// search over offs followed by cu_seqlens (a chain of dependent loads that every one of
+// the chunk's HV blocks would repeat). One thread per chunk.
+__global__ void __launch_bounds__(256) chunk_table_kernel(const PrefillParams p,
+                                                          const int64_t* __restrict__ offs,
+                                                          int64_t* __restrict__ table) {
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  const int64_t total = offs[p.N];
+  if (g >= total || total > unit_capacity(p)) return;
+  int64_t lo = 0, hi = p.N;  // the last n with offs[n] <= g
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (offs[mid] <= g) lo = mid;
+    else hi = mid - 1;
+  }
+  int64_t start, end;
+  seq_bounds(p, lo, start, end);
+  const int64_t cs = start + (g - offs[lo]) * kC;
+  const int64_t L = (end - cs) < kC ? (end - cs) : kC;
+  table[g] = cs * 128 + L;
+}
+
 // ------------------------------------------------------------------ scan order
 // order[i] = the sequence the i-th group of scan blocks processes: longest first
 // (most chunks), ties by index, so that the longest chains start in the first wave
@@ -208,7 +232,8 @@ constexpr int kPrepThreads = 256;
 
 __global__ void __launch_bounds__(kPrepThreads, 4)
     prep_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
-                const int64_t* __restrict__ offs, uint8_t* __restrict__ a2_out) {
+                const int64_t* __restrict__ offs, const int64_t* __restrict__ table,
+                uint8_t* __restrict__ a2_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align_smem<1024>(smem_raw);
   float* sAf = reinterpret_cast<float*>(sm + P_OFF_AF);
@@ -223,19 +248,10 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
   const int h = static_cast<int>(blockIdx.x % p.HV);
   const int64_t gchunk = blockIdx.x / p.HV;
   const int64_t total = offs[p.N];
+  const int64_t entry = gchunk < unit_capacity(p) ? table[gchunk] : 0;
   if (gchunk >= total || total > unit_capacity(p)) return;  // (overflow: nothing written)
-  // sequence containing this chunk: the last n with offs[n] <= gchunk
-  int64_t lo = 0, hi = p.N;
-  while (lo < hi) {
-    const int64_t mid = (lo + hi + 1) >> 1;
-    if (offs[mid] <= gchunk) lo = mid;
-    else hi = mid - 1;
-  }
-  const int64_t n = lo;
-  int64_t start, end;
-  seq_bounds(p, n, start, end);
-  const int64_t cs = start + (gchunk - offs[n]) * kC;
-  const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
+  const int64_t cs = entry >> 7;
+  const int L = static_cast<int>(entry & 127);
   const int qh = h / (p.HV / p.HQ);
 
   if (t == 0) {
@@ -776,13 +792,23 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
     int o_L = 0;
     auto store_output = [&]() {
       __nv_bfloat16* dst = p.out + (o_cs * HV + h) * kHeadDim + v;
+      const int64_t row = HV * kHeadDim;
+      dst += static_cast<int64_t>(16 * ch) * row;
+      if (o_L == kC) {  // full chunk (uniform): no per-token predicate
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int ii = 16 * ch + i;
-        const uint32_t w = opk[i >> 1];
-        if (ii < o_L)
-          dst[static_cast<int64_t>(ii) * HV * kHeadDim] =
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t w = opk[i >> 1];
+          dst[i * row] =
               __ushort_as_bfloat16(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xffffu)));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t w = opk[i >> 1];
+          if (16 * ch + i < o_L)
+            dst[i * row] = __ushort_as_bfloat16(
+                static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xffffu)));
+        }
       }
     };
 #ifdef GDN_PHASE_PROFILE
@@ -980,15 +1006,18 @@ bool encode_v_map(CUtensorMap* map, const void* base, int64_t T, int HV) {
 
 }  // namespace
 
-// Workspace: [0, 256) status word; [256, ...) chunk offsets (N + 1 int64), then the
-// scan order (N int32); then, 1024-aligned, 24 KB of [T_b; P] per (chunk, v-head).
-static size_t head_bytes(int64_t N) {
-  return (256 + 8 * static_cast<size_t>(N + 1) + 4 * static_cast<size_t>(N) + 1023) &
+// Workspace: [0, 256) status word; [256, ...) chunk offsets (N + 1 int64), the scan
+// order (N int32, padded to 8 B), the chunk table (ceil(T / 64) + N int64); then,
+// 1024-aligned, 24.5 KB of [T_b; P] and gates per (chunk, v-head).
+static size_t order_bytes(int64_t N) { return (4 * static_cast<size_t>(N) + 7) & ~size_t(7); }
+static size_t head_bytes(int64_t T, int64_t N) {
+  const size_t chunks = static_cast<size_t>((T + kC - 1) / kC + N);
+  return (256 + 8 * static_cast<size_t>(N + 1) + order_bytes(N) + 8 * chunks + 1023) &
          ~size_t(1023);
 }
 
 size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV) {
-  const size_t head = head_bytes(N);
+  const size_t head = head_bytes(T, N);
   const size_t chunks = static_cast<size_t>((T + kC - 1) / kC + N);
   return head + chunks * static_cast<size_t>(HV) * kUnitBytes;
 }
@@ -998,7 +1027,8 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int64_t* offs = reinterpret_cast<int64_t*>(ws + 256);
   int32_t* order = reinterpret_cast<int32_t*>(ws + 256 + 8 * (p.N + 1));
-  const size_t head = head_bytes(p.N);
+  int64_t* table = reinterpret_cast<int64_t*>(ws + 256 + 8 * (p.N + 1) + order_bytes(p.N));
+  const size_t head = head_bytes(p.T, p.N);
   uint8_t* a2 = ws + head;
   ChunkTmaps maps;
   const int64_t Tm = p.T > 0 ? p.T : 1;
@@ -1013,7 +1043,10 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
                                                                                  order);
   const int64_t cap = (p.T + kC - 1) / kC + p.N;
   if (p.T > 0) {
-    prep_kernel<<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(p, maps, offs, a2);
+    chunk_table_kernel<<<static_cast<unsigned>((cap + 255) / 256), 256, 0, stream>>>(p, offs,
+                                                                                   table);
+    prep_kernel<<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(
+        p, maps, offs, table, a2);
   }
   ScanMaps smaps;
   smaps.k = maps.k;
