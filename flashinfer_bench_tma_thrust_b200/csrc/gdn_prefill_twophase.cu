@@ -185,6 +185,68 @@ __global__ void __launch_bounds__(256) chunk_table_kernel(const PrefillParams p,
   table[g] = cs * 128 + L;
 }
 
+// ------------------------------------------------------------------ chunk gates
+// One warp per (chunk, v-head), tokens l and l + 32 per lane: the gates (accurate
+// softplus / exp / sigmoid), the in-chunk cumulative log2 decay G_j (an inclusive scan
+// of each half of the chunk, the first half's total added to the second — the same
+// operations in the same order as a two-warp scan) and beta_j. Written into the unit:
+// the scan's gates (gamma_j = 2^{G_j}, f_j = 2^{G_last - G_j}) at their place after
+// the image, and G_j, beta_j for the prep in the image's first 512 bytes (the prep
+// reads them first and overwrites them with T_b later). Taking this off the prep
+// blocks removes two block-wide barriers and the gate arithmetic (two warps busy while
+// six wait) from the start of every prep block.
+__global__ void __launch_bounds__(256) chunk_gates_kernel(const PrefillParams p,
+                                                          const int64_t* __restrict__ offs,
+                                                          const int64_t* __restrict__ table,
+                                                          uint8_t* __restrict__ a2_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int64_t gchunk = gw / p.HV;
+  const int h = static_cast<int>(gw % p.HV);
+  const int64_t total = offs[p.N];
+  if (gchunk >= total || total > unit_capacity(p)) return;
+  const int64_t entry = table[gchunk];
+  const int64_t cs = entry >> 7;
+  const int L = static_cast<int>(entry & 127);
+  const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
+  const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
+  const bool v0 = lane < L, v1 = lane + 32 < L;
+  float ra0 = 0.f, rb0 = 0.f, ra1 = 0.f, rb1 = 0.f;
+  if (v0) {
+    ra0 = load_scalar(p.a, p.a_dtype, (cs + lane) * p.HV + h);
+    rb0 = load_scalar(p.b, p.b_dtype, (cs + lane) * p.HV + h);
+  }
+  if (v1) {
+    ra1 = load_scalar(p.a, p.a_dtype, (cs + lane + 32) * p.HV + h);
+    rb1 = load_scalar(p.b, p.b_dtype, (cs + lane + 32) * p.HV + h);
+  }
+  float x0 = v0 ? gate_log_decay(A_log, ra0, dtb) * kLog2e : 0.0f;
+  float x1 = v1 ? gate_log_decay(A_log, ra1, dtb) * kLog2e : 0.0f;
+  const float b0 = v0 ? gate_beta(rb0) : 0.0f, b1 = v1 ? gate_beta(rb1) : 0.0f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+    const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+    if (lane >= o) {
+      x0 += y0;
+      x1 += y1;
+    }
+  }
+  x1 += __shfl_sync(0xffffffffu, x0, 31);
+  const float glast = __shfl_sync(0xffffffffu, x1, 31);
+  uint8_t* unit = a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) * kUnitBytes;
+  float* gp = reinterpret_cast<float*>(unit);
+  gp[lane] = x0;
+  gp[lane + 32] = x1;
+  gp[kC + lane] = b0;
+  gp[kC + lane + 32] = b1;
+  float* gd = reinterpret_cast<float*>(unit + kA2Bytes);
+  gd[lane] = ex2(x0);
+  gd[lane + 32] = ex2(x1);
+  gd[kC + lane] = v0 ? ex2(glast - x0) : 0.0f;
+  gd[kC + lane + 32] = v1 ? ex2(glast - x1) : 0.0f;
+}
+
 // ------------------------------------------------------------------ scan order
 // order[i] = the sequence the i-th group of scan blocks processes: longest first
 // (most chunks), ties by index, so that the longest chains start in the first wave
@@ -250,8 +312,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
   const int64_t total = offs[p.N];
   const int64_t entry = gchunk < unit_capacity(p) ? table[gchunk] : 0;
   if (gchunk >= total || total > unit_capacity(p)) return;  // (overflow: nothing written)
-  const int64_t cs = entry >> 7;
-  const int L = static_cast<int>(entry & 127);
+  const int64_t cs = entry >> 7;  // (the chunk's length, entry & 127, is the gates kernel's)
   const int qh = h / (p.HV / p.HQ);
 
   if (t == 0) {
@@ -266,13 +327,12 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
     tma_load_3d(sm + P_OFF_KQ + 16384 + 8192, &maps.q, bar_tma, 64, qh, tok);
   }
   if (warp == 0) tmem_alloc(tmem_slot, kPrepTmemCols);
-  float ra = 0.f, rb = 0.f;
-  if (t < kC && t < L) {
-    ra = load_scalar(p.a, p.a_dtype, (cs + t) * p.HV + h);
-    rb = load_scalar(p.b, p.b_dtype, (cs + t) * p.HV + h);
+  if (t < kC) {  // G_j and beta_j, written into this unit by chunk_gates_kernel
+    const float* gp = reinterpret_cast<const float*>(
+        a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) * kUnitBytes);
+    sG[t] = gp[t];
+    sBeta[t] = gp[kC + t];
   }
-  const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
-  const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -280,13 +340,6 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
   const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + c0;
 
   PPHASE_INIT;
-  chunk_gates(ra, rb, L, A_log, dtb, sG, sBeta);
-  if (t < kC) {  // the scan's gates: gamma_j = e^{Gamma_j}, f_j = e^{Gamma_last - Gamma_j}
-    float* gdst = reinterpret_cast<float*>(a2_out + (static_cast<uint64_t>(gchunk) * p.HV + h) *
-                                                        kUnitBytes + kA2Bytes);
-    gdst[t] = ex2(sG[t]);
-    gdst[kC + t] = (t < L) ? ex2(sG[kC - 1] - sG[t]) : 0.0f;
-  }
   PPHASE(0);  // gates
   bool ok = mbar_wait(bar_tma, 0);
   PPHASE(1);  // TMA wait
@@ -1045,6 +1098,8 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   if (p.T > 0) {
     chunk_table_kernel<<<static_cast<unsigned>((cap + 255) / 256), 256, 0, stream>>>(p, offs,
                                                                                    table);
+    chunk_gates_kernel<<<static_cast<unsigned>((cap * p.HV + 7) / 8), 256, 0, stream>>>(
+        p, offs, table, a2);
     prep_kernel<<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(
         p, maps, offs, table, a2);
   }

@@ -188,5 +188,5 @@ def kernel_fused(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
 
 def launches_per_call() -> int:
     """Kernel launches one ``kernel()`` call makes (chunk offsets, scan order, chunk
-    table, prep, scan)."""
-    return 5
+    table, chunk gates, prep, scan)."""
+    return 6
