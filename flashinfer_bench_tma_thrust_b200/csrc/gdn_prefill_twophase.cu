@@ -112,8 +112,9 @@ __device__ __forceinline__ void seq_bounds(const PrefillParams& p, int64_t n, in
 
 // ------------------------------------------------------------------ chunk offsets
 // offs[n] = number of 64-token chunks in sequences 0..n-1 (offs[0] = 0). One block.
+constexpr int64_t kInlineSortN = 1024;  // scan order computed by this kernel up to here
 __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams p,
-                                                             int64_t* offs) {
+                                                             int64_t* offs, int32_t* order) {
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t carry;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -159,30 +160,22 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
     __syncthreads();
   }
   if (t == 0 && carry > unit_capacity(p) && p.status) atomicOr(p.status, kStatusBadSeqlens);
-}
-
-// ------------------------------------------------------------------ chunk table
-// table[g] = cs * 128 + L for every chunk g < offs[N]: its first token cs and its length
-// L (1..64), so that each prep block finds its chunk with one load instead of a binary
-// search over offs followed by cu_seqlens (a chain of dependent loads that every one of
-// the chunk's HV blocks would repeat). One thread per chunk.
-__global__ void __launch_bounds__(256) chunk_table_kernel(const PrefillParams p,
-                                                          const int64_t* __restrict__ offs,
-                                                          int64_t* __restrict__ table) {
-  const int64_t g = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  const int64_t total = offs[p.N];
-  if (g >= total || total > unit_capacity(p)) return;
-  int64_t lo = 0, hi = p.N;  // the last n with offs[n] <= g
-  while (lo < hi) {
-    const int64_t mid = (lo + hi + 1) >> 1;
-    if (offs[mid] <= g) lo = mid;
-    else hi = mid - 1;
+  if (p.N <= kInlineSortN) {
+    // the scan order (as scan_order_kernel: longest first, ties by index), one sequence
+    // per thread over chunk counts held in shared memory; saves that kernel's launch
+    __shared__ int64_t s_cnt[kInlineSortN];
+    if (t < p.N) s_cnt[t] = offs[t + 1] - offs[t];  // this block's own writes, synced above
+    __syncthreads();
+    if (t < p.N) {
+      const int64_t cn = s_cnt[t];
+      int64_t rank = 0;
+      for (int64_t m = 0; m < p.N; ++m) {
+        const int64_t cm = s_cnt[m];
+        rank += (cm > cn || (cm == cn && m < t)) ? 1 : 0;
+      }
+      order[rank] = static_cast<int32_t>(t);
+    }
   }
-  int64_t start, end;
-  seq_bounds(p, lo, start, end);
-  const int64_t cs = start + (g - offs[lo]) * kC;
-  const int64_t L = (end - cs) < kC ? (end - cs) : kC;
-  table[g] = cs * 128 + L;
 }
 
 // ------------------------------------------------------------------ chunk gates
@@ -197,7 +190,7 @@ __global__ void __launch_bounds__(256) chunk_table_kernel(const PrefillParams p,
 // six wait) from the start of every prep block.
 __global__ void __launch_bounds__(256) chunk_gates_kernel(const PrefillParams p,
                                                           const int64_t* __restrict__ offs,
-                                                          const int64_t* __restrict__ table,
+                                                          int64_t* __restrict__ table,
                                                           uint8_t* __restrict__ a2_out) {
   const int lane = threadIdx.x & 31;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
@@ -205,9 +198,18 @@ __global__ void __launch_bounds__(256) chunk_gates_kernel(const PrefillParams p,
   const int h = static_cast<int>(gw % p.HV);
   const int64_t total = offs[p.N];
   if (gchunk >= total || total > unit_capacity(p)) return;
-  const int64_t entry = table[gchunk];
-  const int64_t cs = entry >> 7;
-  const int L = static_cast<int>(entry & 127);
+  int64_t lo = 0, hi = p.N;  // the sequence holding the chunk: the last n with offs[n] <= g
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (offs[mid] <= gchunk) lo = mid;
+    else hi = mid - 1;
+  }
+  int64_t start, end;
+  seq_bounds(p, lo, start, end);
+  const int64_t cs = start + (gchunk - offs[lo]) * kC;
+  const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
+  // the chunk table entry for the prep blocks: first token and length
+  if (h == 0 && lane == 0) table[gchunk] = cs * 128 + L;
   const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
   const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
   const bool v0 = lane < L, v1 = lane + 32 < L;
@@ -1091,13 +1093,12 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
   if (cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
       cudaSuccess)
     return -1;
-  chunk_offsets_kernel<<<1, 1024, 0, stream>>>(p, offs);
-  scan_order_kernel<<<static_cast<unsigned>((p.N + 255) / 256), 256, 0, stream>>>(p.N, offs,
-                                                                                 order);
+  chunk_offsets_kernel<<<1, 1024, 0, stream>>>(p, offs, order);
+  if (p.N > kInlineSortN)
+    scan_order_kernel<<<static_cast<unsigned>((p.N + 255) / 256), 256, 0, stream>>>(p.N, offs,
+                                                                                   order);
   const int64_t cap = (p.T + kC - 1) / kC + p.N;
   if (p.T > 0) {
-    chunk_table_kernel<<<static_cast<unsigned>((cap + 255) / 256), 256, 0, stream>>>(p, offs,
-                                                                                   table);
     chunk_gates_kernel<<<static_cast<unsigned>((cap * p.HV + 7) / 8), 256, 0, stream>>>(
         p, offs, table, a2);
     prep_kernel<<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(

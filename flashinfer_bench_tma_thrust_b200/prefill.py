@@ -186,7 +186,8 @@ def kernel_fused(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
     return run_chunked(P, out, new_state, fused=True)
 
 
-def launches_per_call() -> int:
-    """Kernel launches one ``kernel()`` call makes (chunk offsets, scan order, chunk
-    table, chunk gates, prep, scan)."""
-    return 6
+def launches_per_call(n_seqs: int = 1) -> int:
+    """Kernel launches one ``kernel()`` call over ``n_seqs`` sequences makes: chunk
+    offsets (with the scan order up to 1024 sequences), chunk gates (with the chunk
+    table), prep, scan; plus a separate scan-order launch above 1024 sequences."""
+    return 4 if n_seqs <= 1024 else 5

@@ -169,7 +169,7 @@ GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* 
  *
  * q, k, v and out must be 16-byte aligned (q/k are read by TMA); T < 2^31.
  * Stream-ordered launches, no host synchronisation (two-phase path: chunk offsets,
- * scan order, chunk table, chunk gates, prep, scan; fused path: one kernel); the work runs in fp32 on the state
+ * chunk gates, prep, scan; fused path: one kernel); the work runs in fp32 on the state
  * with tensor-core products carried as bf16 hi/lo pairs (about 16 significant bits).
  */
 GDN_API size_t gdn_prefill_chunked_workspace_size(int64_t T, int64_t N, int32_t HV);

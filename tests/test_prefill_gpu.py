@@ -100,6 +100,22 @@ def test_chunked_vs_recurrent_long_sequence():
     assert_state_close(s1, s2, PREFILL_STATE_ATOL, "chunked vs recurrent, 32768 tokens")
 
 
+@pytest.mark.parametrize("n_seqs", [1024, 1100])
+def test_chunked_many_sequences(n_seqs):
+    """Many short ragged sequences (empty ones included) on both sides of the 1024-sequence
+    limit up to which the chunk-offsets kernel also computes the scan order (above it a
+    separate launch does): the chunked path agrees with the token-sequential kernel."""
+    g = torch.Generator().manual_seed(n_seqs)
+    lengths = torch.randint(0, 80, (n_seqs,), generator=g).tolist()
+    x = W.prefill_inputs(lengths, seed=5, gen_device="cuda", device="cuda")
+    o1, s1 = prefill.kernel(*x.args())
+    o2, s2 = prefill.kernel_recurrent(*x.args())
+    assert_out_close(o1, o2, f"chunked vs recurrent, {n_seqs} sequences")
+    assert_state_close(s1, s2, PREFILL_STATE_ATOL, f"chunked vs recurrent, {n_seqs} sequences")
+    torch.cuda.synchronize()
+    assert prefill.device_status() == 0
+
+
 def test_chunked_status_word_clean():
     """Every bounded wait inside the chunked kernel completed in the calls above."""
     x = to_dev(W.prefill_inputs([130, 7], HQ=2, HV=4, seed=31))
