@@ -343,22 +343,30 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
 
   PPHASE_INIT;
   PPHASE(0);  // gates
-  bool ok = mbar_wait(bar_tma, 0);
-  PPHASE(1);  // TMA wait
-  sync_before_mma();
-  if (__syncthreads_and(ok)) {
-    if (t < 32) {  // warp 0 issues
+  // S = [K;Q] K^T: only the K/Q tile (TMA-written) feeds it, so warp 0 issues it as
+  // soon as its own wait for the copy returns, with no block-wide barrier; every thread
+  // then waits for the MMA's completion before the tile's space is reused
+  bool ok = true;
+  if (t < 32) {
+    ok = mbar_wait(bar_tma, 0);
+    if (__all_sync(0xffffffffu, ok)) {
       const Operand kq{smem_u32(sm + P_OFF_KQ), 0, false, 0, 0, 16384};
       issue_gemm(tmem + PT_S, kq, kq, ID_KK, 8);
       mma_commit_w(bar_mma);
     }
-    ok = mbar_wait(bar_mma, 0);
-    tc_fence_after();
-    PPHASE(2);  // S MMA
-    if (__syncthreads_and(ok)) {
-      // the K/Q tile is dead: M and A reuse its space
+  }
+  PPHASE(1);  // TMA wait
+  ok = mbar_wait(bar_mma, 0) && ok;
+  tc_fence_after();
+  PPHASE(2);  // S MMA
+  {
+    {
+      // the K/Q tile is dead: M and A reuse its space (after a failed wait this reads
+      // stale TMEM, and the barrier below stops the block)
       build_a_m_256<PadLayout>(trow + PT_S, sAf, sG, sBeta, sm + P_OFF_M_HI, sm + P_OFF_M_LO);
-      __syncthreads();
+    }
+    ok = __syncthreads_and(ok);  // (so that thread 0 reports a failure seen by any thread)
+    if (ok) {
       PPHASE(3);  // build A, M
       solve_tb_256<PadLayout>(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
       PPHASE(4);  // solve + T_b
