@@ -24,6 +24,9 @@
 // A tiny first kernel turns cu_seqlens into per-sequence chunk offsets so that
 // no host synchronisation is needed.
 #include "gdn_chunk_common.cuh"
+#include <cstdlib>
+#include <mutex>
+
 #include "gdn_launch.h"
 
 namespace gdn {
@@ -114,7 +117,8 @@ __device__ __forceinline__ void seq_bounds(const PrefillParams& p, int64_t n, in
 // offs[n] = number of 64-token chunks in sequences 0..n-1 (offs[0] = 0). One block.
 constexpr int64_t kInlineSortN = 1024;  // scan order computed by this kernel up to here
 __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams p,
-                                                             int64_t* offs, int32_t* order) {
+                                                             int64_t* offs, int32_t* order,
+                                                             int64_t* eoffs, int split_q) {
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t carry;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -175,6 +179,16 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
       }
       order[rank] = static_cast<int32_t>(t);
     }
+    if (split_q > 0 && t == 0) {
+      // split call: sequence n's first floor(cnt_n split_q / 1024) chunks are "early"
+      // (prep before the scan's first part); eoffs = their prefix sums
+      int64_t e = 0;
+      eoffs[0] = 0;
+      for (int64_t n = 0; n < p.N; ++n) {
+        e += (s_cnt[n] * split_q) >> 10;
+        eoffs[n + 1] = e;
+      }
+    }
   }
 }
 
@@ -191,7 +205,10 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const PrefillParams
 __global__ void __launch_bounds__(256) chunk_gates_kernel(const PrefillParams p,
                                                           const int64_t* __restrict__ offs,
                                                           int64_t* __restrict__ table,
-                                                          uint8_t* __restrict__ a2_out) {
+                                                          uint8_t* __restrict__ a2_out,
+                                                          const int64_t* __restrict__ eoffs,
+                                                          longlong2* __restrict__ elist,
+                                                          longlong2* __restrict__ llist) {
   const int lane = threadIdx.x & 31;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int64_t gchunk = gw / p.HV;
@@ -208,8 +225,17 @@ __global__ void __launch_bounds__(256) chunk_gates_kernel(const PrefillParams p,
   seq_bounds(p, lo, start, end);
   const int64_t cs = start + (gchunk - offs[lo]) * kC;
   const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
-  // the chunk table entry for the prep blocks: first token and length
-  if (h == 0 && lane == 0) table[gchunk] = cs * 128 + L;
+  // the chunk table entry for the prep blocks: first token and length; in a split call
+  // also the chunk's place in the early or the late unit list
+  if (h == 0 && lane == 0) {
+    table[gchunk] = cs * 128 + L;
+    if (eoffs) {
+      const int64_t k = gchunk - offs[lo], spn = eoffs[lo + 1] - eoffs[lo];
+      const longlong2 e = make_longlong2(gchunk, cs * 128 + L);
+      if (k < spn) elist[eoffs[lo] + k] = e;
+      else llist[(offs[lo] - eoffs[lo]) + (k - spn)] = e;
+    }
+  }
   const float A_log = load_scalar(p.A_log, p.A_log_dtype, h);
   const float dtb = load_scalar(p.dt_bias, p.dt_bias_dtype, h);
   const bool v0 = lane < L, v1 = lane + 32 < L;
@@ -294,10 +320,12 @@ constexpr uint32_t kPrepTmemCols = 128;
 constexpr uint32_t PT_S = 0, PT_P = 64;
 constexpr int kPrepThreads = 256;
 
+template <int mode>
 __global__ void __launch_bounds__(kPrepThreads, 4)
     prep_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps,
                 const int64_t* __restrict__ offs, const int64_t* __restrict__ table,
-                uint8_t* __restrict__ a2_out) {
+                uint8_t* __restrict__ a2_out, const int64_t* __restrict__ eoffs,
+                const longlong2* __restrict__ list) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align_smem<1024>(smem_raw);
   float* sAf = reinterpret_cast<float*>(sm + P_OFF_AF);
@@ -310,10 +338,20 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
 
   const int t = threadIdx.x, warp = t >> 5, r = t & 127, c0 = (t >> 7) * 32;
   const int h = static_cast<int>(blockIdx.x % p.HV);
-  const int64_t gchunk = blockIdx.x / p.HV;
-  const int64_t total = offs[p.N];
-  const int64_t entry = gchunk < unit_capacity(p) ? table[gchunk] : 0;
-  if (gchunk >= total || total > unit_capacity(p)) return;  // (overflow: nothing written)
+  int64_t gchunk, entry;
+  if constexpr (mode == 0) {  // every unit, in chunk order
+    gchunk = blockIdx.x / p.HV;
+    const int64_t total = offs[p.N];
+    entry = gchunk < unit_capacity(p) ? table[gchunk] : 0;
+    if (gchunk >= total || total > unit_capacity(p)) return;  // (overflow: nothing written)
+  } else {  // split call: the early (mode 1) or late (mode 2) units, from their list
+    const int64_t pos = blockIdx.x / p.HV;
+    const int64_t total = offs[p.N], ne = eoffs[p.N];
+    if (total > unit_capacity(p) || pos >= (mode == 1 ? ne : total - ne)) return;
+    const longlong2 e = list[pos];
+    gchunk = e.x;
+    entry = e.y;
+  }
   const int64_t cs = entry >> 7;  // (the chunk's length, entry & 127, is the gates kernel's)
   const int qh = h / (p.HV / p.HQ);
 
@@ -582,10 +620,11 @@ constexpr uint32_t TP_S = 0;
 constexpr uint32_t TP_D1 = 128;  // 2 x 128
 constexpr uint32_t TP_GO = 384;  // G2's result [U^T | (PX)^T]
 
+template <int mode>
 __global__ void __launch_bounds__(kScanWThreads, 1)
     scan_w_kernel(const PrefillParams p, const __grid_constant__ ScanMaps maps,
                   const int64_t* __restrict__ offs, const int32_t* __restrict__ order,
-                  const uint8_t* __restrict__ a2_in) {
+                  const uint8_t* __restrict__ a2_in, const int64_t* __restrict__ eoffs) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align_smem<1024>(smem_raw);
   uint64_t* bar_kq = reinterpret_cast<uint64_t*>(sm + Q_OFF_BAR);  // [3] K/Q tiles
@@ -616,6 +655,19 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   const int64_t HV = p.HV;
   int64_t start, end;
   seq_bounds(p, n, start, end);
+  // a split call's first part (mode 1) runs the sequence's early chunks, the second part
+  // (mode 2) the rest from the state the first part wrote
+  int64_t k0 = 0;
+  if (mode != 0 && end > start) {  // (mode: compile-time)
+    const int64_t spn = eoffs[n + 1] - eoffs[n];
+    if (mode == 1) {
+      const int64_t e1 = start + spn * kC;
+      end = e1 < end ? e1 : end;
+    } else {
+      k0 = spn;
+      start += spn * kC;
+    }
+  }
 
   const bool skip = end <= start || offs[p.N] > unit_capacity(p);
   // this thread's quarter of state row v: S[n, h, v, 32c .. 32c+32)
@@ -654,7 +706,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
 
   if (issuer) {
     // ================================ MMA / copy issuer ================================
-    const uint8_t* a2_seq = a2_in + static_cast<uint64_t>(offs[n]) * HV * kUnitBytes +
+    const uint8_t* a2_seq = a2_in + static_cast<uint64_t>(offs[n] + k0) * HV * kUnitBytes +
                             static_cast<uint64_t>(h) * kUnitBytes;
     const uint64_t a2_chunk_stride = static_cast<uint64_t>(HV) * kUnitBytes;
     const bool leader = (t & 31) == 0;
@@ -1073,10 +1125,71 @@ bool encode_v_map(CUtensorMap* map, const void* base, int64_t T, int HV) {
 // order (N int32, padded to 8 B), the chunk table (ceil(T / 64) + N int64); then,
 // 1024-aligned, 24.5 KB of [T_b; P] and gates per (chunk, v-head).
 static size_t order_bytes(int64_t N) { return (4 * static_cast<size_t>(N) + 7) & ~size_t(7); }
-static size_t head_bytes(int64_t T, int64_t N) {
+// ... then the early-chunk prefix (N + 1 int64) and, 16-byte aligned, the early and late
+// unit lists (16 B per chunk each) of a split call.
+struct WsLayout {
+  size_t offs, order, table, eoffs, elist, llist, head;
+};
+static WsLayout ws_layout(int64_t T, int64_t N) {
   const size_t chunks = static_cast<size_t>((T + kC - 1) / kC + N);
-  return (256 + 8 * static_cast<size_t>(N + 1) + order_bytes(N) + 8 * chunks + 1023) &
-         ~size_t(1023);
+  WsLayout w;
+  w.offs = 256;
+  w.order = w.offs + 8 * static_cast<size_t>(N + 1);
+  w.table = w.order + order_bytes(N);
+  w.eoffs = w.table + 8 * chunks;
+  w.elist = (w.eoffs + 8 * static_cast<size_t>(N + 1) + 15) & ~size_t(15);
+  w.llist = w.elist + 16 * chunks;
+  w.head = (w.llist + 16 * chunks + 1023) & ~size_t(1023);
+  return w;
+}
+static size_t head_bytes(int64_t T, int64_t N) { return ws_layout(T, N).head; }
+
+// Split calls. When the scan's (sequence, v-head) chains leave SMs idle (one scan block
+// per SM), the prep of each sequence's last chunks runs on those SMs while the scan
+// works through the first ones: prep (early units, all SMs) -> scan part 1 on the
+// caller's stream (dispatched first, as the in-stream successor) || prep (late units) on a
+// low-priority side stream, behind an event -> scan part 2 on the caller's stream.
+// Only stream order and events between the launches; no kernel waits on another.
+struct SplitStreams {
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_prep = nullptr, ev_scan = nullptr;
+  int sms = 0;
+};
+static std::mutex g_split_mutex;
+static SplitStreams g_split[64];
+
+static SplitStreams* split_streams() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_split_mutex);
+  SplitStreams& s = g_split[dev];
+  if (!s.side) {
+    int lo = 0, hi = 0;
+    if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess) return nullptr;
+    if (cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return nullptr;
+    if (cudaStreamCreateWithPriority(&s.side, cudaStreamNonBlocking, lo) != cudaSuccess) {
+      s.side = nullptr;
+      return nullptr;
+    }
+    if (cudaEventCreateWithFlags(&s.ev_prep, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s.ev_scan, cudaEventDisableTiming) != cudaSuccess)
+      return nullptr;
+  }
+  return &s;
+}
+
+// Fraction (of 1024) of each sequence's chunks prepped before the scan starts, or 0 for
+// no split: the late prep runs on the `idle` SMs during the first scan part and must keep
+// ahead of it: (1 - f) P sms / idle <= f S, with S / P ~ 1.4 (scan vs prep time of a call
+// on all SMs, measured). Needs >= 8 idle SMs and >= 64 chunks per sequence on average.
+static int split_fraction(const PrefillParams& p, int sms) {
+  const char* env = getenv("GDN_PREFILL_OVERLAP");
+  if (env && env[0] == '0') return 0;
+  const int64_t chains = p.N * p.HV, idle = sms - chains;
+  if (p.N > kInlineSortN || idle < 8 || p.T < 64 * kC * p.N) return 0;
+  const double r = static_cast<double>(sms) / static_cast<double>(idle);
+  return static_cast<int>(1024.0 * r / (r + 1.4));
 }
 
 size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV) {
@@ -1088,40 +1201,76 @@ size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV) {
 int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_t stream) {
   if (p.N == 0) return 0;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  int64_t* offs = reinterpret_cast<int64_t*>(ws + 256);
-  int32_t* order = reinterpret_cast<int32_t*>(ws + 256 + 8 * (p.N + 1));
-  int64_t* table = reinterpret_cast<int64_t*>(ws + 256 + 8 * (p.N + 1) + order_bytes(p.N));
-  const size_t head = head_bytes(p.T, p.N);
+  const WsLayout wl = ws_layout(p.T, p.N);
+  int64_t* offs = reinterpret_cast<int64_t*>(ws + wl.offs);
+  int32_t* order = reinterpret_cast<int32_t*>(ws + wl.order);
+  int64_t* table = reinterpret_cast<int64_t*>(ws + wl.table);
+  const int64_t cap = (p.T + kC - 1) / kC + p.N;
+  int64_t* eoffs = reinterpret_cast<int64_t*>(ws + wl.eoffs);
+  longlong2* elist = reinterpret_cast<longlong2*>(ws + wl.elist);
+  longlong2* llist = reinterpret_cast<longlong2*>(ws + wl.llist);
+  const size_t head = wl.head;
   uint8_t* a2 = ws + head;
   ChunkTmaps maps;
   const int64_t Tm = p.T > 0 ? p.T : 1;
   const void* kb = p.T > 0 ? static_cast<const void*>(p.k) : static_cast<const void*>(p.new_state);
   const void* qb = p.T > 0 ? static_cast<const void*>(p.q) : static_cast<const void*>(p.new_state);
   if (!encode_qk_map(&maps.k, kb, Tm, p.HQ) || !encode_qk_map(&maps.q, qb, Tm, p.HQ)) return -2;
-  if (cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
-      cudaSuccess)
+  if (cudaFuncSetAttribute(prep_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(prep_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(prep_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
+          cudaSuccess)
     return -1;
-  chunk_offsets_kernel<<<1, 1024, 0, stream>>>(p, offs, order);
+  SplitStreams* ss = p.T > 0 ? split_streams() : nullptr;
+  const int split_q = ss ? split_fraction(p, ss->sms) : 0;
+  chunk_offsets_kernel<<<1, 1024, 0, stream>>>(p, offs, order, eoffs, split_q);
   if (p.N > kInlineSortN)
     scan_order_kernel<<<static_cast<unsigned>((p.N + 255) / 256), 256, 0, stream>>>(p.N, offs,
                                                                                    order);
-  const int64_t cap = (p.T + kC - 1) / kC + p.N;
   if (p.T > 0) {
     chunk_gates_kernel<<<static_cast<unsigned>((cap * p.HV + 7) / 8), 256, 0, stream>>>(
-        p, offs, table, a2);
-    prep_kernel<<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(
-        p, maps, offs, table, a2);
+        p, offs, table, a2, split_q ? eoffs : nullptr, elist, llist);
+    if (!split_q)
+      prep_kernel<0><<<static_cast<unsigned>(cap * p.HV), kPrepThreads, kPrepSmem, stream>>>(
+          p, maps, offs, table, a2, eoffs, elist);
   }
   ScanMaps smaps;
   smaps.k = maps.k;
   smaps.q = maps.q;
   const void* vb = p.T > 0 ? static_cast<const void*>(p.v) : static_cast<const void*>(p.new_state);
   if (!encode_v_map(&smaps.v, vb, Tm, p.HV)) return -2;
-  if (cudaFuncSetAttribute(scan_w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kScanWSmem) != cudaSuccess)
+  for (auto fn : {scan_w_kernel<0>, scan_w_kernel<1>, scan_w_kernel<2>})
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanWSmem) !=
+        cudaSuccess)
+      return -1;
+  const unsigned scan_grid = static_cast<unsigned>(p.N * p.HV);
+  if (!split_q) {
+    scan_w_kernel<0><<<scan_grid, kScanWThreads, kScanWSmem, stream>>>(p, smaps, offs, order,
+                                                                      a2, eoffs);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  }
+  // early units (at most cap * f of them), then the first scan part on the side stream
+  // while the late units (at most cap (1 - f) + N) are prepped on the caller's stream
+  const int64_t n_early = cap * split_q / 1024 + 1;
+  const int64_t n_late = cap - cap * split_q / 1024 + p.N + 1;
+  prep_kernel<1><<<static_cast<unsigned>(n_early * p.HV), kPrepThreads, kPrepSmem, stream>>>(
+      p, maps, offs, table, a2, eoffs, elist);
+  if (cudaEventRecord(ss->ev_prep, stream) != cudaSuccess ||
+      cudaStreamWaitEvent(ss->side, ss->ev_prep, 0) != cudaSuccess)
     return -1;
-  scan_w_kernel<<<static_cast<unsigned>(p.N * p.HV), kScanWThreads, kScanWSmem, stream>>>(
-      p, smaps, offs, order, a2);
+  scan_w_kernel<1><<<scan_grid, kScanWThreads, kScanWSmem, stream>>>(p, smaps, offs, order,
+                                                                    a2, eoffs);
+  prep_kernel<2><<<static_cast<unsigned>(n_late * p.HV), kPrepThreads, kPrepSmem, ss->side>>>(
+      p, maps, offs, table, a2, eoffs, llist);
+  if (cudaEventRecord(ss->ev_scan, ss->side) != cudaSuccess ||
+      cudaStreamWaitEvent(stream, ss->ev_scan, 0) != cudaSuccess)
+    return -1;
+  PrefillParams p2 = p;
+  p2.state = p.new_state;  // the second part continues from the first part's states
+  scan_w_kernel<2><<<scan_grid, kScanWThreads, kScanWSmem, stream>>>(p2, smaps, offs, order,
+                                                                    a2, eoffs);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

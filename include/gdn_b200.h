@@ -169,7 +169,13 @@ GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* 
  *
  * q, k, v and out must be 16-byte aligned (q/k are read by TMA); T < 2^31.
  * Stream-ordered launches, no host synchronisation (two-phase path: chunk offsets,
- * chunk gates, prep, scan; fused path: one kernel); the work runs in fp32 on the state
+ * chunk gates, prep, scan; fused path: one kernel). When the (sequence, v-head) scan
+ * chains leave at least 8 SMs idle and sequences average 64+ chunks, the two-phase call
+ * is split: the prep of each sequence's last chunks runs on a low-priority side stream
+ * of the library (one per device, created on the first such call, with two events)
+ * concurrently with the first part of the scan, joined back into `stream` by an event
+ * before the scan's second part; environment variable GDN_PREFILL_OVERLAP=0 turns this
+ * off. The work runs in fp32 on the state
  * with tensor-core products carried as bf16 hi/lo pairs (about 16 significant bits).
  */
 GDN_API size_t gdn_prefill_chunked_workspace_size(int64_t T, int64_t N, int32_t HV);

@@ -116,6 +116,23 @@ def test_chunked_many_sequences(n_seqs):
     assert prefill.device_status() == 0
 
 
+def test_split_call_matches_unsplit(monkeypatch):
+    """Few long sequences (4 x 8192 tokens, 32 v-heads: 128 scan chains, SMs left idle):
+    the call is split (the prep of each sequence's last chunks overlaps the first part
+    of the scan) and must agree with the unsplit call (GDN_PREFILL_OVERLAP=0): the state
+    chain is the same fp32 arithmetic; the output of the first chunk after the split
+    takes its state product in one piece instead of two."""
+    x = W.prefill_inputs([8192] * 4, seed=13, gen_device="cuda", device="cuda")
+    monkeypatch.setenv("GDN_PREFILL_OVERLAP", "0")
+    o1, s1 = prefill.kernel(*x.args())
+    monkeypatch.setenv("GDN_PREFILL_OVERLAP", "1")
+    o2, s2 = prefill.kernel(*x.args())
+    torch.cuda.synchronize()
+    assert_out_close(o2, o1, "split vs unsplit")
+    assert_state_close(s2, s1, PREFILL_STATE_ATOL, "split vs unsplit")
+    assert prefill.device_status() == 0
+
+
 def test_chunked_status_word_clean():
     """Every bounded wait inside the chunked kernel completed in the calls above."""
     x = to_dev(W.prefill_inputs([130, 7], HQ=2, HV=4, seed=31))
