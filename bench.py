@@ -320,7 +320,7 @@ def run_ours(args, world, rank, local):
                        "global_tokens": T * world, "parallelism": f"sequence-sharded x{world}",
                        "l2": "inputs (q/k/v >= 100 MB per GPU) larger than L2; no flush"},
             "roofline": pm["roofline"], "clocks": pm["clocks"],
-            "gpu_launches": K * prefill.launches_per_call(len(lengths)),
+            "gpu_launches": K * prefill.launches_per_call(len(lengths), T, 32),
         })
         if world == 1 and rank == 0 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_prefill_baseline(lengths)

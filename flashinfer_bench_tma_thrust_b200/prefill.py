@@ -186,8 +186,16 @@ def kernel_fused(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
     return run_chunked(P, out, new_state, fused=True)
 
 
-def launches_per_call(n_seqs: int = 1) -> int:
-    """Kernel launches one ``kernel()`` call over ``n_seqs`` sequences makes: chunk
-    offsets (with the scan order up to 1024 sequences), chunk gates (with the chunk
-    table), prep, scan; plus a separate scan-order launch above 1024 sequences."""
-    return 4 if n_seqs <= 1024 else 5
+def launches_per_call(n_seqs: int = 1, T: int = 0, HV: int = 32, sms: int | None = None) -> int:
+    """Kernel launches one ``kernel()`` call over ``n_seqs`` sequences of ``T`` tokens in
+    total makes: chunk offsets (with the scan order up to 1024 sequences), chunk gates
+    (with the chunk table), prep, scan; a separate scan-order launch above 1024
+    sequences; and a second prep and scan when the call is split (the library's rule:
+    n_seqs * HV scan chains leave >= 8 of the GPU's ``sms`` idle, >= 64 chunks per
+    sequence on average, GDN_PREFILL_OVERLAP not 0)."""
+    import os
+    if sms is None:
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    split = (os.environ.get("GDN_PREFILL_OVERLAP", "1")[:1] != "0" and n_seqs <= 1024
+             and sms - n_seqs * HV >= 8 and T >= 64 * 64 * n_seqs)
+    return (4 if n_seqs <= 1024 else 5) + (2 if split else 0)

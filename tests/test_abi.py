@@ -65,3 +65,17 @@ def test_prefill_validation_without_gpu(cuda_lib):
     assert call(D=256) == -2
     assert call(T=-1) == -1
     assert call(N=0) == 0
+
+
+def test_prefill_launch_count_rule(monkeypatch):
+    """Launches per chunked-prefill call (the bench's gpu_launches): 4, plus a scan-order
+    launch above 1024 sequences, plus a second prep and scan for split calls (few long
+    sequences leaving SMs idle)."""
+    from flashinfer_bench_tma_thrust_b200 import prefill as P
+    monkeypatch.delenv("GDN_PREFILL_OVERLAP", raising=False)
+    assert P.launches_per_call(4, 4 * 32768, 32, sms=148) == 6     # long config: split
+    assert P.launches_per_call(8, 19679, 32, sms=148) == 4         # varlen: 256 chains
+    assert P.launches_per_call(4, 4 * 1000, 32, sms=148) == 4      # too short to split
+    assert P.launches_per_call(2000, 10**6, 1, sms=148) == 5       # separate scan order
+    monkeypatch.setenv("GDN_PREFILL_OVERLAP", "0")
+    assert P.launches_per_call(4, 4 * 32768, 32, sms=148) == 4
