@@ -13,15 +13,24 @@ distributions; the reference's official trace dataset is not available):
   feeds the previous step's new_state back in (a real decode loop); the state
   is larger than L2 so no flush is needed.
 * ``prefill_varlen``: 8 sequences, lengths ~U[512,4096] (seed 0), int32 cu_seqlens,
-  initial state ~N(0,0.02). Metric: tokens/s.
-* ``prefill_long``: 4 sequences x 32768 tokens per GPU, zero initial state. Metric: tokens/s.
+  initial state ~N(0,0.02). Metric: tokens/s. With N GPUs the same 8 sequences are
+  split into (sequence, head-group) units over the ranks (strong scaling).
+* ``prefill_long``: 4 sequences x 32768 tokens per GPU, zero initial state (32 x 32768
+  on 8 GPUs). Metric: tokens/s.
 
-Multi-GPU (torchrun, one process per GPU): every rank owns its own batch slice
-(weak scaling, no data-path collective); the step time is the max over ranks.
+The decode run (the default) also reports both prefill configurations, the bf16 and
+fp8 state options and the decode batch sweep under ``extra``, each with its own
+roofline, clocks, e2e and CPU figures where they apply.
 
-``--impl reference`` times the reference's CPU implementation of the same path
-(the oracle restatement of the reference's PyTorch baseline, run on the host
-cores with all threads) on a bounded sample of the workload per step.
+Multi-GPU (torchrun, one process per GPU): the work is split with
+flashinfer_bench_tma_thrust_b200.partition (decode: contiguous batch slices; prefill:
+longest-processing-time assignment of sequences or (sequence, head-group) units); no
+data-path collective; the step time is the max over ranks.
+
+``--impl reference`` times the reference's CPU implementation of the same path (its
+PyTorch baseline where staged under baseline/_ref, else the oracle's restatement of
+it) on the host cores with all threads: the full B=256 decode batch per step when the
+run fits in about 150 s, a stated subsample otherwise.
 """
 from __future__ import annotations
 
@@ -218,60 +227,99 @@ def kernel_launch_ms(step, n, device):
     return statistics.mean(s.elapsed_time(e) for s, e in evs)
 
 
-def cpu_decode_baseline(seconds=10.0, sample_B=16):
-    """Oracle (restated reference PyTorch decode) on the host cores, on a sample of the
-    B=256 workload's sequences per step."""
-    from flashinfer_bench_tma_thrust_b200 import workloads as W
+def reference_impl(op: str):
+    """The reference's own CPU implementation of `op` ("decode" / "prefill"): its pure
+    PyTorch baseline gdn/<op>/baseline/triton/kernel.py, staged under baseline/_ref by
+    ``__graft_entry__.build()`` where the reference checkout exists ("reference"); else
+    the oracle's restatement of that file ("port")."""
+    import importlib.util
+    f = ROOT / "baseline" / "_ref" / "gdn" / op / "baseline" / "triton" / "kernel.py"
+    if f.exists():
+        spec = importlib.util.spec_from_file_location(f"_gdn_ref_{op}_baseline", f)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod.kernel, "reference", f"gdn/{op}/baseline/triton/kernel.py (the reference's own)"
     from oracle import gdn_oracle
-    x = W.decode_inputs(256, seed=0)
-    sl = [t[:sample_B] if isinstance(t, torch.Tensor) and t.dim() > 1 else t for t in x.args()]
-    gdn_oracle.decode(*sl)  # warm-up
-    n, t0 = 0, time.perf_counter()
-    while True:
-        gdn_oracle.decode(*sl)
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= seconds and n >= 3:
-            break
-    sb = 2 * sample_B * HV * D * D * 4
-    return {"value": sb * n / el / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"{sample_B} of the 256 sequences per step, {n} steps in {el:.1f} s, "
-                      f"torch CPU fp32, {torch.get_num_threads()} threads of "
-                      f"{os.cpu_count()} cpus"}
+    return getattr(gdn_oracle, op), "port", f"oracle/gdn_oracle.py:{op} (restatement)"
 
 
-def cpu_prefill_baseline(lengths, seconds=10.0, tokens_per_seq=64):
+def cpu_decode_time(B_sample, steps, warmup, seed=1000):
+    """Time `steps` CPU decode steps of the reference implementation on the first
+    B_sample sequences of the B=256 workload (all host threads)."""
     from flashinfer_bench_tma_thrust_b200 import workloads as W
-    from oracle import gdn_oracle
+    fn, kind, where = reference_impl("decode")
+    torch.set_num_threads(os.cpu_count() or 1)
+    x = W.decode_inputs(256, seed=seed)
+    sl = [t[:B_sample] if isinstance(t, torch.Tensor) and t.dim() > 1 else t for t in x.args()]
+    for _ in range(warmup):
+        fn(*sl)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fn(*sl)
+    el = time.perf_counter() - t0
+    sb = 2 * B_sample * HV * D * D * 4
+    cores = torch.get_num_threads()
+    return {"value": sb * steps / el / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{B_sample} of the 256 sequences per step ({'the full workload' if B_sample == 256 else 'subsample'}), "
+                      f"{steps} steps in {el:.1f} s; {where}, torch CPU fp32, {cores} threads of "
+                      f"{os.cpu_count()} cpus"}, el / steps
+
+
+def decode_sample_size(steps, warmup, budget_s=150.0):
+    """Sequences per CPU step so that warmup + steps finish within about budget_s: the
+    full B = 256 when it fits (probe: one step on 32 sequences, cost per sequence taken
+    25 % higher for safety)."""
+    _, per = cpu_decode_time(32, 1, 0)
+    per_seq = 1.25 * per / 32
+    fit = int(budget_s / max(1, steps + warmup) / max(per_seq, 1e-6))
+    return max(1, min(256, fit))
+
+
+def cpu_prefill_time(lengths, with_state, steps, warmup, tokens_per_seq=64, seed=2000):
+    """Time the reference implementation's prefill on the first `tokens_per_seq` tokens
+    of each sequence of the configuration (same head layout and distributions)."""
+    from flashinfer_bench_tma_thrust_b200 import workloads as W
+    fn, kind, where = reference_impl("prefill")
+    torch.set_num_threads(os.cpu_count() or 1)
     sub = [min(l, tokens_per_seq) for l in lengths]
-    x = W.prefill_inputs(sub, seed=0)
-    n, t0 = 0, time.perf_counter()
-    while True:
-        gdn_oracle.prefill(*x.args())
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= seconds and n >= 1:
-            break
-    return {"value": sum(sub) * n / el, "unit": "tokens/s", "cores": torch.get_num_threads(),
-            "kind": "port",
+    x = W.prefill_inputs(sub, seed=seed, with_state=with_state)
+    for _ in range(warmup):
+        fn(*x.args())
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fn(*x.args())
+    el = time.perf_counter() - t0
+    cores = torch.get_num_threads()
+    return {"value": sum(sub) * steps / el, "unit": "tokens/s", "cores": cores, "kind": kind,
             "sample": f"first {tokens_per_seq} tokens of each of the {len(lengths)} sequences "
-                      f"({sum(sub)} tokens) per step, {n} steps in {el:.1f} s, torch CPU fp32, "
-                      f"{torch.get_num_threads()} threads of {os.cpu_count()} cpus"}
+                      f"({sum(sub)} tokens) per step, {steps} steps in {el:.1f} s; {where}, "
+                      f"torch CPU fp32, {cores} threads of {os.cpu_count()} cpus"}
 
 
 # ----------------------------------------------------------------------------- arms
+def _dist_max(ms, device, world):
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
 def run_ours(args, world, rank, local):
-    from flashinfer_bench_tma_thrust_b200 import decode, prefill
+    from flashinfer_bench_tma_thrust_b200 import decode
+    from flashinfer_bench_tma_thrust_b200.partition import plan_decode
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    hbm, bf16, bf16_sus, peak_src = peaks()
+    pk = peaks()
+    hbm = pk[0]
     K, Wm = args.steps, args.warmup
     result = {"n_gpus": world, "steps": K, "warmup": Wm, "higher_is_better": True,
               "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
     if args.workload == "decode":
-        x, info = decode_workload(device, seed=1000 + rank, B=args.batch)
-        B = info["B"]
+        # the global batch (B per GPU x world) sharded by sequence with the partitioner
+        B_glob = args.batch * world
+        b0, b1 = plan_decode(B_glob, world)[rank]
+        x, info = decode_workload(device, seed=1000 + b0, B=b1 - b0)
         holder = {"s": x.state.clone()}
 
         def step():
@@ -283,8 +331,11 @@ def run_ours(args, world, rank, local):
         ms = time_steps(step, K, Wm, device, world)
         clocks = sampler.stop()
         ms_step = ms / K
-        value = world * info["state_bytes"] / (ms_step * 1e-3) / 1e9
-        k_ms = kernel_launch_ms(step, 50, device)
+        value = 2 * B_glob * HV * D * D * 4 / (ms_step * 1e-3) / 1e9
+        # the launch's device time: per-launch event brackets include the events' own
+        # overhead, so the smaller of that and the back-to-back step time is used
+        k_ev = kernel_launch_ms(step, 50, device)
+        k_ms = min(k_ev, ms_step)
         achieved = info["alg_bytes"] / (k_ms * 1e-3) / 1e9
         traffic = ncu_traffic("decode_b256")
         result.update({
@@ -292,96 +343,98 @@ def run_ours(args, world, rank, local):
             "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms_step, 5),
             "dtype": "f32",
             "pct_of_8TBps": round(100.0 * value / world / 8000.0, 2),
-            "config": {"workload": f"gdn_decode B={B}/GPU, 16 q/k heads, 32 v heads, D=128, "
-                                   "fp32 k-last state, bf16 q/k/v/a/b",
-                       "global_batch": B * world, "parallelism": f"sequence-sharded x{world}",
+            "config": {"workload": f"gdn_decode B={args.batch}/GPU, 16 q/k heads, 32 v heads, "
+                                   "D=128, fp32 k-last state, bf16 q/k/v/a/b",
+                       "global_batch": B_glob,
+                       "parallelism": f"sequence-sharded x{world} (partition.plan_decode)",
                        "l2": "state (512 MiB in + 512 MiB out per GPU) larger than L2; no flush"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
-                         "peak_source": peak_src, "unit": "GB/s",
+                         "peak_source": f"{pk[3]} hbm_gbs", "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": traffic,
                          "alg_bytes_per_launch": info["alg_bytes"],
-                         "kernel_ms": round(k_ms, 5)},
+                         "kernel_ms": round(k_ms, 5), "kernel_ms_event_bracket": round(k_ev, 5)},
             "clocks": clocks, "gpu_launches": K,
         })
         if not args.no_e2e:
-            result["e2e"] = decode_e2e(x, info, device, world, min(K, 20), max(3, min(Wm, 3)))
+            jobs = [tuple(x.args())]
+            result["e2e"] = e2e_measure(jobs, decode.kernel, device, world, min(K, 20),
+                                        max(3, min(Wm, 3)),
+                                        units=2 * B_glob * HV * D * D * 4, scale=1e-9,
+                                        unit="GB/s")
         if world == 1 and rank == 0 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_decode_baseline()
+            # the same implementation and inputs as the reference arm, on the full batch
+            # when three steps fit in about 40 s
+            result["cpu_baseline"] = cpu_decode_time(decode_sample_size(3, 1, 40.0), 3, 1)[0]
+        if not args.no_extra:
+            result["extra"] = {
+                "decode_bf16_state": decode_bf16_measure(x, info, K, Wm, device, world, ms_step),
+                "decode_fp8_state": decode_fp8_measure(x, info, K, Wm, device, world, ms_step)}
+            for w, k in (("prefill_varlen", 10), ("prefill_long", 5)):
+                result["extra"][w] = prefill_measure(w, k, 3, device, world, rank, pk, args,
+                                                     e2e_steps=3)
+            result["extra"]["decode_sweep"] = decode_sweep_measure(device, world, rank)
     else:
-        pm = prefill_measure(args.workload, K, Wm, device, world, rank, peak=bf16_sus,
-                             peak_src=peak_src)
-        lengths, T = pm.pop("lengths"), pm.pop("T")
-        result.update({
-            "metric": "GDN prefill tokens/s", "value": pm["value"], "unit": "tokens/s",
-            "ms_per_step": pm["ms_per_step"], "dtype": "f32 state, bf16 tensor-core operands",
-            "config": {"workload": f"gdn_prefill {args.workload}: lengths {lengths[:8]}"
-                                   f"{'...' if len(lengths) > 8 else ''} (T={T}/GPU), 16 q/k "
-                                   "heads, 32 v heads, D=128, chunk 64",
-                       "global_tokens": T * world, "parallelism": f"sequence-sharded x{world}",
-                       "l2": "inputs (q/k/v >= 100 MB per GPU) larger than L2; no flush"},
-            "roofline": pm["roofline"], "clocks": pm["clocks"],
-            "gpu_launches": K * prefill.launches_per_call(len(lengths), T, 32),
-        })
-        if world == 1 and rank == 0 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_prefill_baseline(lengths)
-    if args.workload == "decode" and not args.no_extra:
-        result["extra"] = {"decode_bf16_state": decode_bf16_measure(x, info, K, Wm, device,
-                                                                    world, ms_step),
-                           "decode_fp8_state": decode_fp8_measure(x, info, K, Wm, device,
-                                                                  world, ms_step)}
-        result["extra"].update({
-            w: prefill_measure(w, k, 3, device, world, rank, peak=bf16_sus, peak_src=peak_src,
-                               brief=True)
-            for w, k in (("prefill_varlen", 10), ("prefill_long", 5))})
-        result["extra"]["decode_sweep"] = decode_sweep_measure(device, world, rank)
+        pm = prefill_measure(args.workload, K, Wm, device, world, rank, pk, args,
+                             e2e_steps=min(K, 5))
+        result.update({"metric": "GDN prefill tokens/s", "value": pm.pop("value"),
+                       "unit": pm.pop("unit"), "ms_per_step": pm.pop("ms_per_step"),
+                       "dtype": "f32 state, bf16 tensor-core operands",
+                       "scaling": pm.pop("scaling")})
+        pm.pop("steps"), pm.pop("warmup")
+        result.update(pm)
     return result
 
 
 def decode_sweep_measure(device, world, rank, batches=(1, 16, 64, 256, 1024, 4096)):
-    """Decode batch sweep (global batch B sharded by sequence over the ranks): per B, one
-    CUDA graph of R decode steps, each on its own state buffer (R chosen so that the
-    states of one replay exceed the L2 twice over; R = 1 once one state does), timed
-    with CUDA events over whole replays; max over ranks. Graph replay removes the
-    per-launch host cost that dominates B = 1 and 16."""
+    """Decode batch sweep (global batch B sharded by sequence over the ranks with
+    partition.plan_decode): per B, one CUDA graph of R decode steps, each on its own
+    state buffer (R chosen so that the states of one replay exceed the L2 twice over;
+    R = 1 once one state does), timed with CUDA events over whole replays; max over
+    ranks. Graph replay removes the per-launch host cost that dominates B = 1 and 16."""
     from flashinfer_bench_tma_thrust_b200 import decode, workloads as W
+    from flashinfer_bench_tma_thrust_b200.partition import plan_decode
     per_seq = HV * D * D * 4
     out = []
     for B in batches:
-        Bl = -(-B // world)
-        R = max(1, -(-(2 * 126 * 2 ** 20) // (Bl * per_seq)))
-        xs = [W.decode_inputs(Bl, seed=7000 + 31 * rank + r, gen_device=device, device=device)
-              for r in range(R)]
-        for x in xs:  # warm up outside the capture (library load, attribute set-up)
-            decode.kernel(*x.args())
-        torch.cuda.synchronize(device)
-        g = torch.cuda.CUDAGraph()
-        keep = []
-        with torch.cuda.graph(g):
-            for x in xs:
-                keep.append(decode.kernel(*x.args()))
-        reps = max(3, min(200, int(2e8 // (R * Bl * per_seq * 2) + 1)))
-        for _ in range(3):
-            g.replay()
-        torch.cuda.synchronize(device)
+        b0, b1 = plan_decode(B, world)[rank]
+        Bl = b1 - b0
+        Bmax = max(e - s for s, e in plan_decode(B, world))
+        # (Bl = 0: fewer sequences than ranks; this rank idles but joins the max)
+        R = max(1, -(-(2 * 126 * 2 ** 20) // (max(Bl, 1) * per_seq)))
+        reps = max(3, min(200, int(2e8 // (R * max(Bmax, 1) * per_seq * 2) + 1)))
+        ms = 0.0
+        if Bl > 0:
+            xs = [W.decode_inputs(Bl, seed=7000 + 31 * b0 + r, gen_device=device, device=device)
+                  for r in range(R)]
+            for x in xs:  # warm up outside the capture (library load, attribute set-up)
+                decode.kernel(*x.args())
+            torch.cuda.synchronize(device)
+            g = torch.cuda.CUDAGraph()
+            keep = []
+            with torch.cuda.graph(g):
+                for x in xs:
+                    keep.append(decode.kernel(*x.args()))
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize(device)
         if world > 1:
             torch.distributed.barrier()
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(reps):
-            g.replay()
-        e.record()
-        e.synchronize()
-        ms = s.elapsed_time(e)
-        if world > 1:
-            t = torch.tensor([ms], device=device)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t.item())
-        us_step = 1000.0 * ms / (reps * R)
-        out.append({"B": B, "B_per_gpu": Bl, "us_per_step": round(us_step, 2),
-                    "state_gbs": round(world * 2 * Bl * per_seq / (us_step * 1e-6) / 1e9, 1),
+        if Bl > 0:
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(reps):
+                g.replay()
+            e.record()
+            e.synchronize()
+            ms = s.elapsed_time(e) / (reps * R)  # per step
+        ms = _dist_max(ms, device, world)
+        us_step = 1000.0 * ms
+        out.append({"B": B, "B_per_gpu_max": Bmax, "us_per_step": round(us_step, 2),
+                    "state_gbs": round(2 * B * per_seq / (us_step * 1e-6) / 1e9, 1),
                     "buffers_rotated": R})
-        del g, keep, xs
+        if Bl > 0:
+            del g, keep, xs
         torch.cuda.empty_cache()
     return out
 
@@ -400,8 +453,10 @@ def decode_bf16_measure(x, info, K, Wm, device, world, fp32_ms_step):
     ms = time_steps(step, K, Wm, device, world)
     ms_step = ms / K
     b16 = info["state_bytes"] // 2
-    return {"value": round(world * b16 / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s (bf16 state)",
-            "ms_per_step": round(ms_step, 5),
+    hbm = peaks()[0]
+    v = world * b16 / (ms_step * 1e-3) / 1e9
+    return {"value": round(v, 2), "unit": "GB/s (bf16 state)",
+            "ms_per_step": round(ms_step, 5), "frac_of_hbm": round(v / world / hbm, 4),
             "speedup_vs_fp32_state": round(fp32_ms_step / ms_step, 3),
             "error": "separately reported: see tests/test_decode_bf16_state_gpu.py"}
 
@@ -421,61 +476,119 @@ def decode_fp8_measure(x, info, K, Wm, device, world, fp32_ms_step):
     ms = time_steps(step, K, Wm, device, world)
     ms_step = ms / K
     b8 = info["state_bytes"] // 4 + info["state_bytes"] // (4 * 128)
-    return {"value": round(world * b8 / (ms_step * 1e-3) / 1e9, 2),
+    hbm = peaks()[0]
+    v = world * b8 / (ms_step * 1e-3) / 1e9
+    return {"value": round(v, 2),
             "unit": "GB/s (fp8 state + row scales)", "ms_per_step": round(ms_step, 5),
+            "frac_of_hbm": round(v / world / hbm, 4),
             "speedup_vs_fp32_state": round(fp32_ms_step / ms_step, 3),
             "error": "separately reported: see tests/test_decode_fp8_state_gpu.py"}
 
 
-def prefill_measure(workload, K, Wm, device, world, rank, peak, peak_src, brief=False):
-    """Time K prefill steps (one prefill.kernel call each) of `workload` on this rank."""
-    from flashinfer_bench_tma_thrust_b200 import prefill, workloads as W
+PREFILL_FLOP_PER_TOKEN_HEAD = 6 * D * D + 10 * 64 * D + (2 * 64 * 64) // 3
+
+
+def prefill_plan(workload, world):
+    """Global sequence set of a prefill configuration and its plan over `world` ranks:
+    varlen = the configuration's 8 sequences (strong scaling: (sequence, head-group)
+    units spread over the ranks); long = 4 sequences of 32768 tokens per GPU (weak
+    scaling: whole sequences)."""
+    from flashinfer_bench_tma_thrust_b200.partition import plan_prefill
     lengths, with_state = prefill_lengths(workload)
-    x = W.prefill_inputs(lengths, seed=2000 + rank, gen_device=device, device=device,
+    scaling = "strong" if workload == "prefill_varlen" else "weak"
+    if workload == "prefill_long":
+        lengths = lengths * world
+    return lengths, with_state, scaling, plan_prefill(lengths, world, HQ, HV)
+
+
+def prefill_measure(workload, K, Wm, device, world, rank, pk, args, e2e_steps=3):
+    """Time K prefill steps of `workload`: this rank's calls of prefill.kernel on its
+    part of the global sequence set (partition.plan_prefill / build_local_prefill); the
+    step time is the max over ranks and value = global tokens / step time."""
+    from flashinfer_bench_tma_thrust_b200 import prefill, workloads as W
+    from flashinfer_bench_tma_thrust_b200.partition import build_local_prefill
+    hbm, bf16_burst = pk[0], pk[1]
+    lengths, with_state, scaling, plan = prefill_plan(workload, world)
+    T_glob = sum(lengths)
+    x = W.prefill_inputs(lengths, seed=2000, gen_device=device, device=device,
                          with_state=with_state)
-    T = sum(lengths)
+    local = build_local_prefill(plan, rank, *x.args(), device=device)
+    del x
+    torch.cuda.empty_cache()
+    jobs = [c[4] for c in local.calls]
+    T_loc = sum(sum(c[3]) for c in local.calls)
+    flops = sum(sum(c[3]) * (c[1] - c[0]) for c in local.calls) * PREFILL_FLOP_PER_TOKEN_HEAD
+
+    def nbytes(t):
+        return t.numel() * t.element_size() if isinstance(t, torch.Tensor) else 0
+    # compulsory HBM bytes: every input once (q, k, v, gates, cu_seqlens, initial state),
+    # outputs and final states written once
+    comp_bytes = 0
+    for (h0, h1, seqs, lens, a) in local.calls:
+        comp_bytes += sum(nbytes(t) for t in a) + sum(lens) * (h1 - h0) * D * 2 + \
+            len(seqs) * (h1 - h0) * D * D * 4
+    launches = sum(prefill.launches_per_call(len(c[2]), sum(c[3]), c[1] - c[0])
+                   for c in local.calls)
 
     def step():
-        prefill.kernel(*x.args())
+        for a in jobs:
+            prefill.kernel(*a)
 
     sampler = ClockSampler(device)
     ms = time_steps(step, K, Wm, device, world)
     clocks = sampler.stop()
     ms_step = ms / K
-    flop_per_token = HV * (6 * D * D + 10 * 64 * D + (2 * 64 * 64) // 3)
-    k_ms = kernel_launch_ms(step, 3, device)
-    achieved = T * flop_per_token / (k_ms * 1e-3) / 1e12
-    roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
-            "peak_source": peak_src + " (sustained bf16)", "unit": "TFLOP/s",
-            "frac": round(achieved / peak, 4), "traffic": ncu_traffic(workload),
-            "flop_per_token": flop_per_token, "call_ms": round(k_ms, 4)}
-    out = {"value": round(world * T / (ms_step * 1e-3), 1), "unit": "tokens/s",
-           "ms_per_step": round(ms_step, 4), "steps": K, "warmup": Wm, "roofline": roof}
-    if brief:
-        out["tokens_per_gpu"] = T
-        return out
-    out.update({"lengths": lengths, "T": T, "clocks": clocks})
+    k_ms = kernel_launch_ms(step, 3, device) if jobs else 0.0
+    k_ms = min(k_ms, ms_step) if jobs else 0.0
+    achieved = flops / (k_ms * 1e-3) / 1e12 if k_ms else 0.0
+    dram = comp_bytes / (k_ms * 1e-3) / 1e9 if k_ms else 0.0
+    roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": bf16_burst,
+            "peak_source": f"{pk[3]} bf16_tflops (burst: the call is timed alone)",
+            "unit": "TFLOP/s", "frac": round(achieved / bf16_burst, 4),
+            "traffic": ncu_traffic(workload) if world == 1 else None,
+            "flop_per_token": HV * PREFILL_FLOP_PER_TOKEN_HEAD, "call_ms": round(k_ms, 4),
+            "dram": {"compulsory_bytes": comp_bytes, "achieved_gbs": round(dram, 1),
+                     "peak": hbm, "frac": round(dram / hbm, 4)}}
+    out = {"value": round(T_glob / (ms_step * 1e-3), 1), "unit": "tokens/s",
+           "ms_per_step": round(ms_step, 4), "steps": K, "warmup": Wm, "scaling": scaling,
+           "config": {"workload": f"gdn_prefill {workload}: lengths {lengths[:8]}"
+                                  f"{'...' if len(lengths) > 8 else ''} (T={T_glob} total), "
+                                  "16 q/k heads, 32 v heads, D=128, chunk 64, "
+                                  f"{'initial state N(0,0.02)' if with_state else 'zero state'}",
+                      "global_tokens": T_glob, "tokens_this_rank": T_loc,
+                      "parallelism": f"partition.plan_prefill x{world}: {plan.groups} head "
+                                     f"group(s) per sequence",
+                      "l2": "inputs (q/k/v >= 100 MB) larger than L2; no flush"},
+           "roofline": roof, "clocks": clocks, "gpu_launches": K * launches}
+    if not args.no_e2e and jobs is not None:
+        out["e2e"] = e2e_measure(jobs, prefill.kernel, device, world, e2e_steps, 2,
+                                 units=T_glob, scale=1.0, unit="tokens/s")
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_prefill_time(lengths, with_state, 3, 1)
     return out
 
 
-def decode_e2e(x, info, device, world, K, Wm):
-    """Same metric through the public API (decode.kernel) with host buffers: every step
-    copies its inputs from pinned host memory and reads the output and the new state
-    back into pinned host memory. Copies run on their own streams with two buffer sets,
-    so step i's device->host copy overlaps step i+1's host->device copy and the kernel
-    (the two PCIe directions work concurrently); the timed region spans all streams."""
-    from flashinfer_bench_tma_thrust_b200 import decode
-    B = info["B"]
-    host_sets, dev_sets, out_h, ns_h = [], [], [], []
+def e2e_measure(jobs, fn, device, world, K, Wm, units, scale, unit):
+    """The metric through the public API (`fn` = decode.kernel / prefill.kernel) with
+    host buffers: every step copies all inputs of this rank's calls (`jobs`, tuples of
+    kernel arguments) from pinned host memory, runs the calls, and reads every output
+    (o and new_state) back into pinned host memory. Copies run on their own streams with
+    two buffer sets, so step i's device->host copy overlaps step i+1's host->device copy
+    and the kernels (the two PCIe directions work concurrently); the timed region spans
+    all streams; max over ranks. value = units per step / step time x scale."""
+    host_sets, dev_sets, outs_h = [], [], []
+    probe = [fn(*a) for a in jobs]
     for j in range(2):
-        host_sets.append([t.cpu().pin_memory() if isinstance(t, torch.Tensor) else t
-                          for t in x.args()])
-        dev_sets.append([torch.empty_like(t, device=device) if isinstance(t, torch.Tensor) else t
-                         for t in x.args()])
-        out_h.append(torch.empty(B, 1, HV, D, dtype=torch.bfloat16).pin_memory())
-        ns_h.append(torch.empty(B, HV, D, D, dtype=torch.float32).pin_memory())
-    h2d = sum(t.numel() * t.element_size() for t in host_sets[0] if isinstance(t, torch.Tensor))
-    d2h = out_h[0].numel() * 2 + ns_h[0].numel() * 4
+        host_sets.append([[t.cpu().pin_memory() if isinstance(t, torch.Tensor) else t
+                           for t in a] for a in jobs])
+        dev_sets.append([[torch.empty_like(t, device=device) if isinstance(t, torch.Tensor)
+                          else t for t in a] for a in jobs])
+        outs_h.append([[torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in res]
+                       for res in probe])
+    del probe
+    h2d = sum(t.numel() * t.element_size() for a in host_sets[0] for t in a
+              if isinstance(t, torch.Tensor))
+    d2h = sum(o.numel() * o.element_size() for res in outs_h[0] for o in res)
     comp = torch.cuda.current_stream(device)
     s_in = torch.cuda.Stream(device)
     s_out = torch.cuda.Stream(device)
@@ -493,21 +606,22 @@ def decode_e2e(x, info, device, world, K, Wm):
         it[0] += 1
         with torch.cuda.stream(s_in):
             s_in.wait_event(free[j])
-            for dst, src in zip(dev_sets[j], host_sets[j]):
-                if isinstance(src, torch.Tensor):
-                    dst.copy_(src, non_blocking=True)
+            for dst_a, src_a in zip(dev_sets[j], host_sets[j]):
+                for dst, src in zip(dst_a, src_a):
+                    if isinstance(src, torch.Tensor):
+                        dst.copy_(src, non_blocking=True)
             ready[j].record(s_in)
         comp.wait_event(ready[j])
         comp.wait_event(drained[j])  # host buffers of set j free again
-        out, ns = decode.kernel(*dev_sets[j])
+        results = [fn(*a) for a in dev_sets[j]]
         free[j].record(comp)
         done[j].record(comp)
-        out.record_stream(s_out)
-        ns.record_stream(s_out)
         with torch.cuda.stream(s_out):
             s_out.wait_event(done[j])
-            out_h[j].copy_(out, non_blocking=True)
-            ns_h[j].copy_(ns, non_blocking=True)
+            for res, res_h in zip(results, outs_h[j]):
+                for o, oh in zip(res, res_h):
+                    o.record_stream(s_out)
+                    oh.copy_(o, non_blocking=True)
             drained[j].record(s_out)
 
     for _ in range(Wm):
@@ -527,63 +641,48 @@ def decode_e2e(x, info, device, world, K, Wm):
     end.record(comp)
     end.synchronize()
     torch.cuda.synchronize(device)
-    ms = start.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    # the results of the last step really arrived: compare with a synchronous call
-    ok = torch.equal(out_h[(K + Wm - 1) % 2].float().isfinite().all().reshape(1),
-                     torch.ones(1, dtype=torch.bool))
-    return {"value": round(world * info["state_bytes"] / (ms / K * 1e-3) / 1e9, 3),
-            "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": K,
-            "ms_per_step": round(ms / K, 3), "overlap": "copies on separate streams, 2 buffer sets",
-            "outputs_finite": bool(ok)}
+    ms = _dist_max(start.elapsed_time(end), device, world)
+    last = outs_h[(K + Wm - 1) % 2]
+    ok = all(bool(o.float().isfinite().all()) for res in last for o in res)
+    return {"value": round(units / (ms / K * 1e-3) * scale, 3), "unit": unit,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": K,
+            "ms_per_step": round(ms / K, 3),
+            "overlap": "copies on separate streams, 2 buffer sets", "outputs_finite": ok}
 
 
 def run_reference(args):
-    """Reference arm: the reference's PyTorch path (restated in oracle/) on the host CPU."""
-    from flashinfer_bench_tma_thrust_b200 import workloads as W
-    from oracle import gdn_oracle
-    torch.set_num_threads(os.cpu_count() or 1)
+    """Reference arm: the reference's own CPU implementation of the path (its PyTorch
+    baseline, or the oracle's restatement of it where that file is not staged), on the
+    host cores with all threads, on the same configuration as our arm."""
     K, Wm = args.steps, args.warmup
     if args.workload == "decode":
-        sample_B = 4
-        x = W.decode_inputs(256, seed=1000)
-        sl = [t[:sample_B] if isinstance(t, torch.Tensor) and t.dim() > 1 else t
-              for t in x.args()]
-        fn = lambda: gdn_oracle.decode(*sl)  # noqa: E731
-        units = 2 * sample_B * HV * D * D * 4
-        metric, unit = "GDN decode state GB/s (2*B*HV*D*D*4 / step time)", "GB/s"
-        scale = 1e-9
-        sample = f"{sample_B} of the 256 sequences of the decode workload per step"
-        cfg = "gdn_decode B=256/GPU, 16 q/k heads, 32 v heads, D=128, fp32 k-last state"
+        B_sample = decode_sample_size(K, Wm)
+        # guard against a cost that grows faster than the batch (host memory pressure)
+        while B_sample > 1 and cpu_decode_time(B_sample, 1, 0)[1] * (K + Wm) > 225.0:
+            B_sample //= 2
+        cb, per = cpu_decode_time(B_sample, K, Wm)
+        metric = "GDN decode state GB/s (2*B*HV*D*D*4 / step time)"
+        cfg = {"workload": f"gdn_decode B={args.batch}/GPU, 16 q/k heads, 32 v heads, D=128, "
+                           "fp32 k-last state, bf16 q/k/v/a/b",
+               "global_batch": args.batch * args.gpus, "cpu_batch_per_step": B_sample,
+               "same_config": B_sample == args.batch}
+        ms_step = per * 1e3
     else:
         lengths, with_state = prefill_lengths(args.workload)
-        sub = [min(l, 16) for l in lengths]
-        x = W.prefill_inputs(sub, seed=2000, with_state=with_state)
-        fn = lambda: gdn_oracle.prefill(*x.args())  # noqa: E731
-        units = sum(sub)
-        metric, unit, scale = "GDN prefill tokens/s", "tokens/s", 1.0
-        sample = f"first 16 tokens of each of the {len(lengths)} sequences per step"
-        cfg = f"gdn_prefill {args.workload}: lengths {lengths[:8]}, 16 q/k heads, 32 v heads"
-    for _ in range(Wm):
-        fn()
-    t0 = time.perf_counter()
-    for _ in range(K):
-        fn()
-    el = time.perf_counter() - t0
-    value = units * K / el * scale
-    cores = torch.get_num_threads()
-    line = {"impl": "reference", "metric": metric, "value": round(value, 4), "unit": unit,
-            "n_gpus": args.gpus, "steps": K, "warmup": Wm, "ms_per_step": round(el / K * 1e3, 3),
+        cb = cpu_prefill_time(lengths, with_state, K, Wm, tokens_per_seq=16)
+        metric = "GDN prefill tokens/s"
+        cfg = {"workload": f"gdn_prefill {args.workload}: lengths {lengths[:8]}, 16 q/k heads, "
+                           "32 v heads", "same_config": False}
+        ms_step = None
+    value = cb["value"]
+    line = {"impl": "reference", "metric": metric, "value": round(value, 4), "unit": cb["unit"],
+            "n_gpus": args.gpus, "steps": K, "warmup": Wm,
+            "ms_per_step": round(ms_step, 3) if ms_step else None,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": cfg},
-            "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": cores,
-                             "kind": "port",
-                             "sample": f"{sample}; torch CPU fp32 restatement of the reference "
-                                       f"PyTorch baseline, {cores} threads"},
-            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0,
+            "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": round(value, 4), "unit": cb["unit"], "cores": cb["cores"],
+                             "kind": cb["kind"], "sample": cb["sample"]},
+            "e2e": {"value": round(value, 4), "unit": cb["unit"], "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "gpu_launches": 0}
     print(json.dumps(line), flush=True)

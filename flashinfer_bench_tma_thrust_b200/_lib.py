@@ -59,6 +59,7 @@ SIGNATURES = {
          _p, _int, _f32, _p, _p, _i64, _i64, _i32, _i32, _i32, _p, _size, _p],
     ),
     "gdn_prefill_chunked_status": (_int, [_p, _p, _p]),
+    "gdn_prefill_chunked_launches": (_int, [_i64, _i64, _i32, _size]),
     "gdn_prefill_chunked_fwd_noalloc": (
         _int,
         [_p, _p, _p, _p,

@@ -250,6 +250,15 @@ int gdn_prefill_chunked_fwd(const void* q, const void* k, const void* v, const f
   return launch_status(rc);
 }
 
+int gdn_prefill_chunked_launches(int64_t T, int64_t N, int32_t HV, size_t workspace_bytes) {
+  if (T < 0 || N < 0 || HV <= 0) return GDN_ERR_INVALID_ARG;
+  if (N == 0) return 0;
+  if (workspace_bytes < kChunkedWorkspaceBytes) return GDN_ERR_WORKSPACE;
+  if (workspace_bytes < gdn::prefill_twophase_workspace_bytes(T, N, HV)) return 1;
+  const int n = gdn::prefill_twophase_launches(T, N, HV);
+  return n < 0 ? GDN_ERR_CUDA : n;
+}
+
 int gdn_prefill_chunked_status(const void* workspace, int* host_status, void* stream) {
   if (!workspace || !host_status) return GDN_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -57,5 +57,8 @@ int launch_prefill_recurrent(const PrefillParams& p, cudaStream_t stream);
 int launch_prefill_chunked(const PrefillParams& p, cudaStream_t stream);
 size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV);
 int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_t stream);
+// kernel launches a two-phase call of these sizes makes on the current device (split
+// calls included), or -1 if the device cannot be queried
+int prefill_twophase_launches(int64_t T, int64_t N, int HV);
 
 }  // namespace gdn

@@ -73,22 +73,6 @@ constexpr uint32_t TM_S = 64;    // S = [K;Q] K^T, then [T_b; P]
 constexpr uint32_t TM_1 = 128;   // [KH; QH]
 constexpr uint32_t TM_2 = 192;   // [U; O'], then Kt^T U
 
-#ifdef GDN_PHASE_PROFILE
-// Debug-only phase timer (block 0, thread 0): accumulates clock64 deltas per phase.
-__device__ long long g_phase_cycles[16];
-#define PHASE(i)                                                   \
-  do {                                                             \
-    if (blockIdx.x == 0 && threadIdx.x == 0) {                     \
-      const long long now_ = clock64();                            \
-      g_phase_cycles[i] += now_ - phase_last_;                     \
-      phase_last_ = now_;                                          \
-    }                                                              \
-  } while (0)
-#else
-#define PHASE(i) \
-  do {           \
-  } while (0)
-#endif
 
 __global__ void __launch_bounds__(128, 2)
     prefill_chunked_kernel(const PrefillParams p, const __grid_constant__ ChunkTmaps maps) {
@@ -173,9 +157,6 @@ __global__ void __launch_bounds__(128, 2)
 
   uint32_t tma_phase = 0, mma_phase = 0;
   bool ok = true;
-#ifdef GDN_PHASE_PROFILE
-  long long phase_last_ = clock64();
-#endif
   float ra = 0.f, rb = 0.f;
   issue_tma(start);
   load_gates(start, end, ra, rb);
@@ -185,13 +166,11 @@ __global__ void __launch_bounds__(128, 2)
     const int64_t next = cs + kC;
 
     chunk_gates(ra, rb, L, A_log, dtb, sG, sBeta);
-    PHASE(0);  // gates + scan
     // ---- wait for K/Q, then S = [K;Q] K^T and [KH;QH] = [K;Q] H ----------------------
     ok = mbar_wait(bar_tma, tma_phase);
     tma_phase ^= 1;
     sync_before_mma();
     if (!__syncthreads_and(ok)) break;
-    PHASE(1);  // TMA wait
     if (t < 32) {  // warp 0 issues
       const Operand kq{smem_u32(sm + OFF_KQ), 0, false, 0, 0, 16384};
       const Operand hB{smem_u32(sm + OFF_H_HI), smem_u32(sm + OFF_H_LO), true, 8192, 2048, 0};
@@ -217,7 +196,6 @@ __global__ void __launch_bounds__(128, 2)
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
 
-    PHASE(2);  // S, G1 MMA
     const float g_last = sG[kC - 1];
     build_a_m<SwzLayout>(trow + TM_S, sAf, sG, sBeta, sm + OFF_A2_HI, sm + OFF_A2_LO);
     if (t < kC) {
@@ -238,12 +216,10 @@ __global__ void __launch_bounds__(128, 2)
     }
     __syncthreads();
 
-    PHASE(3);  // A/M/X build
     float nra = 0.f, nrb = 0.f;
     if (next < end) load_gates(next, end, nra, nrb);
 
     solve_tb<SwzLayout>(sAf, sTf, sBeta, sm + OFF_TB_HI, sm + OFF_TB_LO);
-    PHASE(6);  // T_b write
     // ---- [T_b; P] = [I; M] T_b -----------------------------------------------------
     sync_before_mma();
     if (t < 32) {  // warp 0 issues
@@ -256,14 +232,12 @@ __global__ void __launch_bounds__(128, 2)
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
-    PHASE(7);  // P MMA
     {
       float r[64];
       tmem_ld64(trow + TM_S, r);
       store_row_split(sm + OFF_A2_HI, sm + OFF_A2_LO, t, r);
     }
 
-    PHASE(8);  // A2 write
     // ---- [U; O'] = [T_b; P] X ----------------------------------------------------------
     sync_before_mma();
     if (t < 32) {  // warp 0 issues
@@ -276,7 +250,6 @@ __global__ void __launch_bounds__(128, 2)
     mma_phase ^= 1;
     tc_fence_after();
     if (!__syncthreads_and(ok)) break;
-    PHASE(9);  // G2 MMA
     if (t < kC) {
       // f_j U_j with f_j = e^{Gamma_last - Gamma_j} (0 for padded rows): the state
       // update then reads the raw K tile, dH = K^T diag(f) U
@@ -309,7 +282,6 @@ __global__ void __launch_bounds__(128, 2)
       }
     }
 
-    PHASE(10);  // U / O
     // ---- dH = K^T diag(f) U;  H <- gamma_last H + dH ----------------------------------------
     sync_before_mma();
     if (t < 32) {  // warp 0 issues
@@ -324,7 +296,6 @@ __global__ void __launch_bounds__(128, 2)
     if (!__syncthreads_and(ok)) break;
     // the K/Q tile is free: fetch the next chunk while the state is updated
     if (next < end) issue_tma(next);
-    PHASE(11);  // G3 MMA
     {
       float dh[64];
       tmem_ld64(trow + TM_2, dh);
@@ -335,7 +306,6 @@ __global__ void __launch_bounds__(128, 2)
       tmem_st64(trow + TM_H, hrow);
       store_row_split(sm + OFF_H_HI, sm + OFF_H_LO, t, hrow);
     }
-    PHASE(12);  // H update
     ra = nra;
     rb = nrb;
   }
@@ -374,16 +344,3 @@ int launch_prefill_chunked(const PrefillParams& p, cudaStream_t stream) {
 
 }  // namespace gdn
 
-#ifdef GDN_PHASE_PROFILE
-// Debug builds only: copy (and optionally reset) the per-phase cycle counters.
-extern "C" __attribute__((visibility("default"))) int gdn_debug_phase_cycles(long long* host,
-                                                                               int reset) {
-  if (cudaMemcpyFromSymbol(host, gdn::g_phase_cycles, sizeof(long long) * 16) != cudaSuccess)
-    return -1;
-  if (reset) {
-    long long z[16] = {0};
-    if (cudaMemcpyToSymbol(gdn::g_phase_cycles, z, sizeof(z)) != cudaSuccess) return -1;
-  }
-  return 0;
-}
-#endif

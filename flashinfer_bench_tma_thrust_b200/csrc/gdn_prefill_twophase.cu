@@ -39,60 +39,6 @@ constexpr uint32_t kA2Bytes = 24576;     // [T_b; P] image: hi 16 KB | T_b lo 8 
 constexpr uint32_t kGateBytes = 512;     // gamma_j (64 fp32), then f_j (64 fp32)
 constexpr uint32_t kUnitBytes = kA2Bytes + kGateBytes;  // per (chunk, v-head)
 
-#ifdef GDN_PHASE_PROFILE
-// Debug-only phase timer of the scan (block 0, thread 0): clock64 deltas per phase.
-__device__ long long g_scan_cycles[16];
-// (accumulated in shared memory, `sprof_`, and added to g_scan_cycles at exit)
-#define SPHASE(i)                                     \
-  do {                                                \
-    if (blockIdx.x == 0 && threadIdx.x == 0) {        \
-      const long long now_ = clock64();               \
-      sprof_[i] += now_ - sphase_last_;               \
-      sphase_last_ = now_;                            \
-    }                                                 \
-  } while (0)
-#define IPHASE(i)                                     \
-  do {                                                \
-    if (blockIdx.x == 0 && threadIdx.x == 512) {      \
-      const long long now_ = clock64();               \
-      sprof_[8 + (i)] += now_ - iphase_last_;         \
-      iphase_last_ = now_;                            \
-    }                                                 \
-  } while (0)
-// Debug event timestamps of one chunk (block 0, chunk kEventChunk), state thread 0 and
-// the issuer: clock64 values, SM-local.
-__device__ long long g_scan_events[32];
-constexpr int64_t kEventChunk = 100;
-#define SEVENT(i)                                                             \
-  do {                                                                        \
-    if (blockIdx.x == 0 && c == kEventChunk && (threadIdx.x == 0 || threadIdx.x == 512)) \
-      g_scan_events[i] = clock64();                                           \
-  } while (0)
-__device__ long long g_prep_cycles[16];
-#define PPHASE(i)                                     \
-  do {                                                \
-    if (blockIdx.x == 0 && threadIdx.x == 0) {        \
-      const long long now_ = clock64();               \
-      g_prep_cycles[i] += now_ - pphase_last_;        \
-      pphase_last_ = now_;                            \
-    }                                                 \
-  } while (0)
-#define PPHASE_INIT long long pphase_last_ = clock64()
-#else
-#define SPHASE(i) \
-  do {            \
-  } while (0)
-#define PPHASE(i) \
-  do {            \
-  } while (0)
-#define PPHASE_INIT
-#define IPHASE(i) \
-  do {            \
-  } while (0)
-#define SEVENT(i) \
-  do {            \
-  } while (0)
-#endif  // per (chunk, v-head): hi 16 KB + lo rows 0..63 8 KB
 
 // Status word bits (sticky, in the workspace): a bounded wait gave up; cu_seqlens held a
 // value outside [0, T] (used clamped) or ranges whose chunks overflow the workspace
@@ -379,8 +325,6 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
   const uint32_t tmem = *tmem_slot;
   const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + c0;
 
-  PPHASE_INIT;
-  PPHASE(0);  // gates
   // S = [K;Q] K^T: only the K/Q tile (TMA-written) feeds it, so warp 0 issues it as
   // soon as its own wait for the copy returns, with no block-wide barrier; every thread
   // then waits for the MMA's completion before the tile's space is reused
@@ -393,10 +337,8 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
       mma_commit_w(bar_mma);
     }
   }
-  PPHASE(1);  // TMA wait
   ok = mbar_wait(bar_mma, 0) && ok;
   tc_fence_after();
-  PPHASE(2);  // S MMA
   {
     {
       // the K/Q tile is dead: M and A reuse its space (after a failed wait this reads
@@ -405,9 +347,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
     }
     ok = __syncthreads_and(ok);  // (so that thread 0 reports a failure seen by any thread)
     if (ok) {
-      PPHASE(3);  // build A, M
       solve_tb_256<PadLayout>(sAf, sTf, sBeta, sm + P_OFF_TB_HI, sm + P_OFF_TB_LO);
-      PPHASE(4);  // solve + T_b
       sync_before_mma();
       if (t < 32) {  // warp 0 issues  // P = M T_b (result rows 0..63)
         const Operand mA{smem_u32(sm + P_OFF_M_HI), smem_u32(sm + P_OFF_M_LO), false, 0, 0, 0};
@@ -424,10 +364,8 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
         bulk_store(dst + 16384, sm + P_OFF_TB_LO, 8192);
         bulk_commit();
       }
-      PPHASE(5);  // P issue + T_b copy
       ok = mbar_wait(bar_mma, 1);
       tc_fence_after();
-      PPHASE(6);  // P wait
       if (__syncthreads_and(ok) && r < kC) {
         // row r of P -> hi only (P only reaches the bf16 output), rows 64..127 of the hi part
         float pr[32];
@@ -442,7 +380,6 @@ __global__ void __launch_bounds__(kPrepThreads, 4)
               make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-      PPHASE(7);  // P rows write
     }
   }
   if (t == 32) bulk_wait_all();  // the T_b tiles stay in place until copied
@@ -605,9 +542,6 @@ constexpr uint32_t Q_OFF_V = 147456;      // 2 x 16 KB: V tile, rows j x 128 v
 constexpr uint32_t Q_OFF_B = 180224;      // B_c^T image: hi 16 KB (128 rows) | lo 8 KB (K rows)
 constexpr uint32_t Q_OFF_GATES = 204800;  // 2 x (gamma_j, f_j): 2 x 512 B, from the prep
 constexpr uint32_t Q_OFF_BAR = 206848;    // 15 mbarriers, TMEM slot
-#ifdef GDN_PHASE_PROFILE
-constexpr uint32_t Q_OFF_PROF = 206848 + 256;  // debug phase timers (16 x 8 B)
-#endif
 constexpr uint32_t kScanWSmem = 206848 + 512 + 1024;
 // operand g S: thread quarter c writes columns [32c, 32c + 32) as 16 hi words then 16 lo
 // words (K step s: hi at 32 (s/2) + 8 (s%2), lo 16 further); dS (fp32) from G3
@@ -640,10 +574,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   uint64_t* bar_bi = bar_kq + 13;   //              B_c image stored
   uint64_t* bar_o = bar_kq + 14;    //              chunk's output rows read
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Q_OFF_BAR + 128);
-#ifdef GDN_PHASE_PROFILE
-  long long* sprof_ = reinterpret_cast<long long*>(sm + Q_OFF_PROF);
-  if (threadIdx.x < 16) sprof_[threadIdx.x] = 0;
-#endif
 
   const int t = threadIdx.x, warp = t >> 5;
   const bool state_wg = t < kScanWState;
@@ -771,9 +701,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       mma_commit_w(bar_ch);
       if (nch > 1) ok = issue_b(0);
     }
-#ifdef GDN_PHASE_PROFILE
-    long long iphase_last_ = clock64();
-#endif
     for (int64_t c = 0; ok && c < nch; ++c) {
       const bool last = c == nch - 1;
       const int b = static_cast<int>(c & 1);
@@ -786,25 +713,18 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       // U'_{c-1} was signalled
       if (leader && c > 0 && c + 1 < nch) issue_va(c + 1);
       __syncwarp();
-      IPHASE(0);  // loads
-      SEVENT(16);
       // ---- G2_c: D1_c <- X^T [T_b; P]^T = [U^T | (PX)^T] ----------------------------
       ok = mbar_wait_spin(bar_x, ph_x) && ok;
       ph_x ^= 1;
-      SEVENT(24);
       ok = mbar_wait_spin(&bar_va[b], static_cast<uint32_t>((c >> 1) & 1)) && ok;
       tc_fence_after();
       __syncwarp();
       if (!ok) break;
-      IPHASE(1);  // X wait
-      SEVENT(17);
       {
         mma_group_x3(tmem + TP_GO, tmem + d1c, desc_kmajor(smem_u32(a2)),
                      desc_kmajor(smem_u32(a2 + 16384)), 0u);
         mma_commit_w(bar_g2);
       }
-      IPHASE(2);  // G2 issue
-      SEVENT(18);
       if (!last) {
         // ---- G1a_{c+1} = (g_c S_c) [K;Q]_{c+1}^T once the operand is stored -------------
         ok = mbar_wait_spin(bar_op, ph_op) && ok;
@@ -812,21 +732,15 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         tc_fence_after();
         __syncwarp();
         if (!ok) break;
-        IPHASE(3);  // operand wait
-        SEVENT(19);
         // chunk c+2's K/Q tile into chunk c-1's buffer (the third one for c = 0): its
         // last reader G3_{c-1} finished before this operand was signalled
         if (leader && c + 2 < nch) issue_kq(c + 2);
         __syncwarp();
         issue_g1a(d1n, kqn);
         mma_commit_w(bar_g1a);
-        IPHASE(4);  // G1a issue
-        SEVENT(20);
       }
       // ---- U'_c stored: G1'_c onto D1_{c+1}, then G3_c: dS_c = U'^T K_c ----------------
       ok = mbar_wait_spin(bar_u, ph_u) && ok;
-      IPHASE(5);  // U' wait
-      SEVENT(21);
       ph_u ^= 1;
       tc_fence_after();
       __syncwarp();
@@ -853,8 +767,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         mma_commit_w(bar_g3);
       }
       // B_{c+1} for chunk c+1's state-side work (D1_c's buffer is read: U'_c is stored)
-      IPHASE(6);  // G1', G1a wait, G3
-      SEVENT(22);
       // B_{c+1} overwrites the (QH)^T half of D1_c: after the state warps have read
       // chunk c's output rows
       if (c + 2 < nch) {
@@ -866,8 +778,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
           break;
         }
       }
-      IPHASE(7);  // B issue
-      SEVENT(23);
     }
   } else if (state_wg) {
     // ================================ state warps ======================================
@@ -926,9 +836,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         }
       }
     };
-#ifdef GDN_PHASE_PROFILE
-    long long sphase_last_ = clock64();
-#endif
     for (int64_t c = 0; c < nch; ++c) {
       const int64_t cs = start + c * kC;
       const int L = static_cast<int>((end - cs) < kC ? (end - cs) : kC);
@@ -939,15 +846,11 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
       const float* sGam = reinterpret_cast<const float*>(sm + Q_OFF_GATES + b * kGateBytes);
       const float* sF = sGam + kC;
       const uint8_t* vt = sm + Q_OFF_V + b * 16384;
-      SPHASE(0);
-      SEVENT(0);
       // ---- D1_c complete: X_c^T = V^T - (KH)^T diag(gamma), over (KH)^T ------------------
       ok = mbar_wait(bar_ch, ph_ch) && ok;
       ph_ch ^= 1;
       ok = mbar_wait(&bar_va[b], static_cast<uint32_t>((c >> 1) & 1)) && ok;
       tc_fence_after();
-      SPHASE(1);  // D1 wait
-      SEVENT(1);
       {
         float d[16];
         tmem_ld16(lane + d1c + 16 * ch, d);
@@ -967,15 +870,12 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         tmem_st_wait();
       }
       signal(bar_x);
-      SEVENT(2);
-      SPHASE(2);  // X build
 
       // ---- beside the chain: S_c = g_{c-1} S_{c-1} + dS_{c-1}; operand g_c S_c; B_c ------
       if (c > 0) {
         ok = mbar_wait(bar_g3, ph_g3) && ok;  // G3_{c-1}: dS_{c-1}
         ph_g3 ^= 1;
         tc_fence_after();
-        SEVENT(11);
         float d0[32];
         tmem_ld32(lane + TP_S + 32 * ch, d0);
         tmem_ld_wait();
@@ -988,18 +888,14 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         }
       }
       g_prev = sGam[kC - 1];
-      SEVENT(4);
       if (!last) {
         tc_fence_before();
         // every state thread has read dS_{c-1}
         if (!named_bar_and(kStateBar, kScanWState, ok)) break;
         tc_fence_after();
-        SEVENT(5);
         write_s_operand(g_prev);
         signal(bar_op);
-        SEVENT(6);
         ok = mbar_wait(bar_tb, ph_tb) && ok;
-        SEVENT(7);
         ph_tb ^= 1;
         tc_fence_after();
         {
@@ -1022,16 +918,12 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
           }
         }
         signal(bar_bi);
-        SEVENT(8);
       }
-      SPHASE(3);  // state update, operand, B image
 
       // ---- G2_c done: U'^T = U^T diag(f) over X^T; output rows of chunk c ---------------
       ok = mbar_wait(bar_g2, ph_g2) && ok;
       ph_g2 ^= 1;
       tc_fence_after();
-      SPHASE(4);  // G2 wait
-      SEVENT(9);
       {
         float u[16];
         tmem_ld16(lane + TP_GO + 16 * ch, u);
@@ -1050,7 +942,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         tmem_st_wait();
       }
       signal(bar_u);
-      SEVENT(10);
       {
         // O^T row v, tokens i in [16c, 16c+16): scale (gamma_i (QH)^T + (PX)^T), read
         // before B_{c+1} overwrites the (QH)^T half (the issuer waits for bar_o)
@@ -1075,8 +966,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         o_L = L;
       }
       store_output();
-      SEVENT(3);
-      SPHASE(6);  // U' and output rows
     }
     if (ok) {
       ok = mbar_wait(bar_g3, ph_g3);
@@ -1098,9 +987,6 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   if (!ok && p.status) atomicOr(p.status, kStatusWaitTimeout);
   tc_fence_before();
   __syncthreads();
-#ifdef GDN_PHASE_PROFILE
-  if (blockIdx.x == 0 && t < 16) g_scan_cycles[t] += sprof_[t];
-#endif
   if (issuer) tmem_dealloc(tmem, kScanTTmemCols);
 }
 
@@ -1154,27 +1040,44 @@ struct SplitStreams {
   cudaStream_t side = nullptr;
   cudaEvent_t ev_prep = nullptr, ev_scan = nullptr;
   int sms = 0;
+  bool ready = false;
+  // held by a split call from its first event record to the final join, so that calls
+  // from several host threads (on their own streams and workspaces) never interleave
+  // their records and waits on the shared side stream and events
+  std::mutex launch;
 };
 static std::mutex g_split_mutex;
 static SplitStreams g_split[64];
 
+// The device's side stream and events, created on the first split call (both events and
+// the stream, or nothing: a partial creation is undone and the call runs unsplit).
 static SplitStreams* split_streams() {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lock(g_split_mutex);
   SplitStreams& s = g_split[dev];
-  if (!s.side) {
+  if (!s.ready) {
     int lo = 0, hi = 0;
-    if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess) return nullptr;
-    if (cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      return nullptr;
-    if (cudaStreamCreateWithPriority(&s.side, cudaStreamNonBlocking, lo) != cudaSuccess) {
-      s.side = nullptr;
+    if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
+        cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
       return nullptr;
     }
-    if (cudaEventCreateWithFlags(&s.ev_prep, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&s.ev_scan, cudaEventDisableTiming) != cudaSuccess)
+    cudaStream_t side = nullptr;
+    cudaEvent_t e1 = nullptr, e2 = nullptr;
+    const bool ok = cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, lo) == cudaSuccess &&
+                    cudaEventCreateWithFlags(&e1, cudaEventDisableTiming) == cudaSuccess &&
+                    cudaEventCreateWithFlags(&e2, cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+      if (e1) cudaEventDestroy(e1);
+      if (side) cudaStreamDestroy(side);
+      cudaGetLastError();
       return nullptr;
+    }
+    s.side = side;
+    s.ev_prep = e1;
+    s.ev_scan = e2;
+    s.ready = true;
   }
   return &s;
 }
@@ -1196,6 +1099,23 @@ size_t prefill_twophase_workspace_bytes(int64_t T, int64_t N, int HV) {
   const size_t head = head_bytes(T, N);
   const size_t chunks = static_cast<size_t>((T + kC - 1) / kC + N);
   return head + chunks * static_cast<size_t>(HV) * kUnitBytes;
+}
+
+int prefill_twophase_launches(int64_t T, int64_t N, int HV) {
+  if (N <= 0) return 0;
+  int dev = -1, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  PrefillParams p{};
+  p.T = T;
+  p.N = N;
+  p.HV = HV;
+  const int base = N > kInlineSortN ? 4 : 3;  // offsets (+ order), gates, scan (+ prep)
+  if (T <= 0) return base - 1;                // no gates or prep launch
+  return base + 1 + (split_fraction(p, sms) ? 2 : 0);
 }
 
 int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_t stream) {
@@ -1251,8 +1171,9 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
                                                                       a2, eoffs);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
   }
-  // early units (at most cap * f of them), then the first scan part on the side stream
-  // while the late units (at most cap (1 - f) + N) are prepped on the caller's stream
+  // early units (at most cap * f of them), then the first scan part on the caller's
+  // stream while the late units (at most cap (1 - f) + N) are prepped on the side stream
+  std::lock_guard<std::mutex> split_lock(ss->launch);
   const int64_t n_early = cap * split_q / 1024 + 1;
   const int64_t n_late = cap - cap * split_q / 1024 + p.N + 1;
   prep_kernel<1><<<static_cast<unsigned>(n_early * p.HV), kPrepThreads, kPrepSmem, stream>>>(
@@ -1276,30 +1197,3 @@ int launch_prefill_twophase(const PrefillParams& p, void* workspace, cudaStream_
 
 }  // namespace gdn
 
-#ifdef GDN_PHASE_PROFILE
-extern "C" __attribute__((visibility("default"))) int gdn_debug_prep_cycles(long long* host,
-                                                                              int reset) {
-  if (cudaMemcpyFromSymbol(host, gdn::g_prep_cycles, sizeof(long long) * 16) != cudaSuccess)
-    return -1;
-  if (reset) {
-    long long z[16] = {0};
-    if (cudaMemcpyToSymbol(gdn::g_prep_cycles, z, sizeof(z)) != cudaSuccess) return -1;
-  }
-  return 0;
-}
-extern "C" __attribute__((visibility("default"))) int gdn_debug_scan_events(long long* host) {
-  return cudaMemcpyFromSymbol(host, gdn::g_scan_events, sizeof(long long) * 32) == cudaSuccess
-             ? 0
-             : -1;
-}
-extern "C" __attribute__((visibility("default"))) int gdn_debug_scan_cycles(long long* host,
-                                                                              int reset) {
-  if (cudaMemcpyFromSymbol(host, gdn::g_scan_cycles, sizeof(long long) * 16) != cudaSuccess)
-    return -1;
-  if (reset) {
-    long long z[16] = {0};
-    if (cudaMemcpyToSymbol(gdn::g_scan_cycles, z, sizeof(z)) != cudaSuccess) return -1;
-  }
-  return 0;
-}
-#endif

@@ -101,17 +101,23 @@ def kernel_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=Non
 
 
 _workspaces: dict = {}
+# per device: (pinned host int32 copy of the status word, event recorded after the copy)
+_status_probe: dict = {}
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Per-device workspace of the chunked prefill (zeroed once; its first bytes hold
     the sticky status word, the rest the per-chunk units of the two-phase path: the
-    [T_b; P] operand image and the chunk's gates, 24.5 KB per (chunk, v-head)). Grown on demand, never shrunk; calls on one
-    device share it, so they must be ordered on one stream."""
+    [T_b; P] operand image and the chunk's gates, 24.5 KB per (chunk, v-head)). Grown on
+    demand, never shrunk; a grown workspace keeps the status bits set so far. Calls on
+    one device share it, so they must be ordered on one stream."""
     key = (device.type, device.index)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        new = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        if ws is not None:
+            new[:4].copy_(ws[:4])  # stream-ordered: the sticky bits survive the growth
+        ws = new
         _workspaces[key] = ws
     return ws
 
@@ -136,10 +142,16 @@ def device_status(device=None) -> int:
 
 
 def reset_device_status(device=None) -> None:
-    """Clear the sticky status word on `device` (stream-ordered on the current stream)."""
-    ws = _workspaces.get(_device_key(device))
+    """Clear the sticky status word on `device` (stream-ordered on the current stream) and
+    the host copy that the next call checks."""
+    key = _device_key(device)
+    ws = _workspaces.get(key)
     if ws is not None:
         ws[:4].zero_()
+    probe = _status_probe.get(key)
+    if probe is not None:
+        probe[1].synchronize()
+        probe[0].zero_()
 
 
 def _aligned(t):
@@ -171,12 +183,50 @@ def run_chunked(P: _Prepared, out, new_state, fused: bool = False):
     return out, new_state
 
 
-def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
-    """Reference-compatible prefill entry point: one launch of the chunked tensor-core
-    kernel (chunk 64, state carried in fp32 in TMEM)."""
+def _check_status(dev, check: bool) -> None:
+    """Report a failure of a chunked call on `dev`. Every call queues an asynchronous copy
+    of the sticky status word into pinned host memory; the next call on the device reads
+    the copy if it has landed (no synchronisation) and raises GDNError for any bit set.
+    With check=True the call waits for its own copy and raises for its own failure."""
+    key = (dev.type, dev.index)
+    probe = _status_probe.get(key)
+    if probe is not None and (check or probe[1].query()):
+        if check:
+            probe[1].synchronize()
+        st = int(probe[0].item())
+        if st:
+            raise _lib.GDNError(
+                f"gdn_prefill_chunked_fwd reported status bits {st:#x} on {dev} "
+                "(1: a bounded wait gave up; 2: invalid cu_seqlens); the outputs of the "
+                "failing call are invalid. Clear with reset_device_status().")
+
+
+def _queue_status_copy(dev) -> None:
+    key = (dev.type, dev.index)
+    probe = _status_probe.get(key)
+    if probe is None:
+        probe = (torch.zeros(1, dtype=torch.int32).pin_memory(), torch.cuda.Event())
+        _status_probe[key] = probe
+    ws = _workspaces[key]
+    probe[0].copy_(ws[:4].view(torch.int32), non_blocking=True)
+    probe[1].record()
+
+
+def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, *, check=False):
+    """Reference-compatible prefill entry point: one call of the chunked tensor-core
+    kernel (chunk 64, state carried in fp32). A failure that the kernels report through
+    the device status word (a bounded wait that gave up, invalid cu_seqlens) raises
+    GDNError at the next call on the device, or at this call with ``check=True``
+    (which synchronises on the status copy)."""
     P = prepare(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+    _check_status(P.dev, False)
     out, new_state = _alloc_outputs(P)
-    return run_chunked(P, out, new_state)
+    run_chunked(P, out, new_state)
+    with torch.cuda.device(P.dev):
+        _queue_status_copy(P.dev)
+    if check:
+        _check_status(P.dev, True)
+    return out, new_state
 
 
 def kernel_fused(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
@@ -186,16 +236,14 @@ def kernel_fused(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None):
     return run_chunked(P, out, new_state, fused=True)
 
 
-def launches_per_call(n_seqs: int = 1, T: int = 0, HV: int = 32, sms: int | None = None) -> int:
+def launches_per_call(n_seqs: int = 1, T: int = 0, HV: int = 32) -> int:
     """Kernel launches one ``kernel()`` call over ``n_seqs`` sequences of ``T`` tokens in
-    total makes: chunk offsets (with the scan order up to 1024 sequences), chunk gates
-    (with the chunk table), prep, scan; a separate scan-order launch above 1024
-    sequences; and a second prep and scan when the call is split (the library's rule:
-    n_seqs * HV scan chains leave >= 8 of the GPU's ``sms`` idle, >= 64 chunks per
-    sequence on average, GDN_PREFILL_OVERLAP not 0)."""
-    import os
-    if sms is None:
-        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    split = (os.environ.get("GDN_PREFILL_OVERLAP", "1")[:1] != "0" and n_seqs <= 1024
-             and sms - n_seqs * HV >= 8 and T >= 64 * 64 * n_seqs)
-    return (4 if n_seqs <= 1024 else 5) + (2 if split else 0)
+    total makes on the current device, as the library reports it
+    (``gdn_prefill_chunked_launches``): chunk offsets (with the scan order up to 1024
+    sequences), chunk gates, prep, scan; a separate scan-order launch above 1024
+    sequences; a second prep and scan when the call is split."""
+    lib = _lib.load()
+    ws = lib.gdn_prefill_chunked_workspace_size(T, n_seqs, HV)
+    n = lib.gdn_prefill_chunked_launches(T, n_seqs, HV, ws)
+    _lib.check(n if n < 0 else 0, "gdn_prefill_chunked_launches")
+    return n

@@ -175,7 +175,9 @@ GDN_API int gdn_prefill_recurrent_fwd(const void* q, const void* k, const void* 
  * of the library (one per device, created on the first such call, with two events)
  * concurrently with the first part of the scan, joined back into `stream` by an event
  * before the scan's second part; environment variable GDN_PREFILL_OVERLAP=0 turns this
- * off. The work runs in fp32 on the state
+ * off. The side stream and its events are created by the first split call on a device:
+ * make that call before any stream capture on that device. Split calls from several host
+ * threads are safe (a per-device lock orders their event records and waits). The work runs in fp32 on the state
  * with tensor-core products carried as bf16 hi/lo pairs (about 16 significant bits).
  */
 GDN_API size_t gdn_prefill_chunked_workspace_size(int64_t T, int64_t N, int32_t HV);
@@ -188,6 +190,14 @@ GDN_API int gdn_prefill_chunked_fwd(const void* q, const void* k, const void* v,
                                     float* new_state, int64_t T, int64_t N, int32_t HQ,
                                     int32_t HV, int32_t D, void* workspace,
                                     size_t workspace_bytes, void* stream);
+
+/* Number of kernel launches a gdn_prefill_chunked_fwd call with these sizes and this
+ * workspace size makes on the current device: 1 on the fused path; on the two-phase path
+ * 4 (5 above 1024 sequences), plus 2 when the call is split (see above), fewer when
+ * T = 0. No counterpart in the reference (a diagnostic; launches nothing). Returns a
+ * negative status code on bad sizes or if the device cannot be queried. */
+GDN_API int gdn_prefill_chunked_launches(int64_t T, int64_t N, int32_t HV,
+                                         size_t workspace_bytes);
 
 /* Copy the workspace status word (the bit set above) to *host_status (synchronises
  * `stream`). Clearing it is the caller's: it is the workspace's first 4 bytes. */

@@ -67,15 +67,29 @@ def test_prefill_validation_without_gpu(cuda_lib):
     assert call(N=0) == 0
 
 
+def test_prefill_launch_count_validation_without_gpu(cuda_lib):
+    """gdn_prefill_chunked_launches checks its sizes before it queries the device; a
+    workspace below the two-phase size selects the fused path: one launch."""
+    lib = cuda_lib
+    assert lib.gdn_prefill_chunked_launches(100, 0, 32, 1 << 30) == 0
+    assert lib.gdn_prefill_chunked_launches(-1, 1, 32, 1 << 30) == -1
+    assert lib.gdn_prefill_chunked_launches(100, 1, 32, 16) == -5   # workspace too small
+    assert lib.gdn_prefill_chunked_launches(4096, 2, 32, 256) == 1  # fused path
+
+
+@pytest.mark.gpu
 def test_prefill_launch_count_rule(monkeypatch):
-    """Launches per chunked-prefill call (the bench's gpu_launches): 4, plus a scan-order
-    launch above 1024 sequences, plus a second prep and scan for split calls (few long
-    sequences leaving SMs idle)."""
+    """Launches per chunked-prefill call as the library reports them (the bench's
+    gpu_launches): 4, plus a scan-order launch above 1024 sequences, plus a second prep
+    and scan for split calls (few long sequences leaving SMs idle; values for 148 SMs)."""
+    import torch
     from flashinfer_bench_tma_thrust_b200 import prefill as P
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("launch counts below are for a 148-SM B200")
     monkeypatch.delenv("GDN_PREFILL_OVERLAP", raising=False)
-    assert P.launches_per_call(4, 4 * 32768, 32, sms=148) == 6     # long config: split
-    assert P.launches_per_call(8, 19679, 32, sms=148) == 4         # varlen: 256 chains
-    assert P.launches_per_call(4, 4 * 1000, 32, sms=148) == 4      # too short to split
-    assert P.launches_per_call(2000, 10**6, 1, sms=148) == 5       # separate scan order
+    assert P.launches_per_call(4, 4 * 32768, 32) == 6     # long config: split
+    assert P.launches_per_call(8, 19679, 32) == 4         # varlen: 256 chains
+    assert P.launches_per_call(4, 4 * 1000, 32) == 4      # too short to split
+    assert P.launches_per_call(2000, 10**6, 1) == 5       # separate scan order
     monkeypatch.setenv("GDN_PREFILL_OVERLAP", "0")
-    assert P.launches_per_call(4, 4 * 32768, 32, sms=148) == 4
+    assert P.launches_per_call(4, 4 * 32768, 32) == 4

@@ -7,11 +7,87 @@ from flashinfer_bench_tma_thrust_b200 import prefill, workloads as W
 from golden import golden
 from oracle import gdn_oracle
 from parity import (PREFILL_STATE_ATOL, STATE_REL_FROB, assert_out_close, assert_state_close,
-                    to_dev)
+                    state_errors, to_dev)
 
 pytestmark = pytest.mark.gpu
 
 PRE_CASES = [c for c in golden.case_names() if c.startswith("pre_")]
+
+def _report(name, out, ref_out, ns, ref_ns, extra=None):
+    """Append the parity figures of a full-size case to $GDN_PARITY_REPORT (JSON lines)
+    when that variable names a file; the assertions do not depend on it."""
+    import json
+    import os
+    path = os.environ.get("GDN_PARITY_REPORT")
+    if not path:
+        return
+    o, r = out.detach().float().cpu(), ref_out.detach().float().cpu()
+    err, rel = state_errors(ns, ref_ns)
+    rec = {"case": name, "out_max_abs": (o - r).abs().max().item(),
+           "out_rel_frob": ((o - r).norm() / r.norm().clamp_min(1e-30)).item(),
+           "state_max_abs": err, "state_rel_frob": rel}
+    rec.update(extra or {})
+    with open(path, "a") as f:
+        f.write(json.dumps(rec) + "\n")
+
+
+# ---- the benchmark configurations against the CPU oracle (first in this file) ---------
+def test_chunked_vs_oracle_varlen_config():
+    """Config 4 in full: 8 sequences with lengths ~U[512, 4096] (seed 0), int32
+    cu_seqlens, initial state N(0, 0.02), 16/32 heads; the chunked kernel (and the fused
+    single-kernel path) against the CPU oracle (the reference's PyTorch recurrence,
+    restated) on the same inputs. The oracle takes a few seconds per 10K tokens."""
+    lengths = W.varlen_lengths(seed=0)
+    x = W.prefill_inputs(lengths, seed=0, cu_dtype=torch.int32)
+    assert x.cu_seqlens.dtype == torch.int32 and x.state is not None
+    ref_out, ref_ns = gdn_oracle.prefill(*x.args())
+    xd = to_dev(x)
+    for name, fn in (("chunked", prefill.kernel), ("fused", prefill.kernel_fused)):
+        out, ns = fn(*xd.args())
+        torch.cuda.synchronize()
+        _report(f"varlen_config_{name}", out, ref_out, ns, ref_ns, {"T": sum(lengths)})
+        assert_out_close(out, ref_out, f"varlen config, {name} vs oracle")
+        assert_state_close(ns, ref_ns, PREFILL_STATE_ATOL, f"varlen config, {name} vs oracle")
+    assert prefill.device_status() == 0
+
+
+def _seq_slice(x, n):
+    """Inputs of sequence n of a packed prefill input alone (cu_seqlens [0, L])."""
+    import dataclasses
+    cu = [int(c) for c in x.cu_seqlens.tolist()]
+    s, e = cu[n], cu[n + 1]
+    vals = {f.name: getattr(x, f.name) for f in dataclasses.fields(x)}
+    for key in ("q", "k", "v", "a", "b"):
+        vals[key] = vals[key][s:e]
+    vals["cu_seqlens"] = torch.tensor([0, e - s], dtype=x.cu_seqlens.dtype)
+    if vals["state"] is not None:
+        vals["state"] = vals["state"][n:n + 1]
+    return type(x)(**vals), s, e
+
+
+def test_chunked_vs_oracle_long_config_split(monkeypatch):
+    """Config 5's 1-GPU run in full (4 sequences x 32768 tokens, zero initial state,
+    16/32 heads), through the split-call path (128 scan chains leave SMs idle, so the
+    prep of each sequence's late chunks overlaps the scan: asserted through the
+    library's launch count), against the CPU oracle on the first and the last sequence
+    (the oracle costs ~10 s per 32768 tokens; every sequence runs the same code)."""
+    monkeypatch.delenv("GDN_PREFILL_OVERLAP", raising=False)
+    lengths = [32768] * 4
+    x = W.prefill_inputs(lengths, seed=2000, with_state=False)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if sms - 4 * 32 >= 8:
+        assert prefill.launches_per_call(4, sum(lengths), 32) == 6, "call not split"
+    out, ns = prefill.kernel(*to_dev(x).args())
+    torch.cuda.synchronize()
+    for n in (0, 3):
+        xs, s, e = _seq_slice(x, n)
+        ref_out, ref_ns = gdn_oracle.prefill(*xs.args())
+        _report(f"long_config_seq{n}", out[s:e], ref_out, ns[n:n + 1], ref_ns, {"T": e - s})
+        assert_out_close(out[s:e], ref_out, f"long config, sequence {n} vs oracle")
+        assert_state_close(ns[n:n + 1], ref_ns, PREFILL_STATE_ATOL,
+                           f"long config, sequence {n} vs oracle")
+    assert prefill.device_status() == 0
+
 IMPLS = {"chunked": prefill.kernel, "fused": prefill.kernel_fused,
          "recurrent": prefill.kernel_recurrent}
 
@@ -123,7 +199,11 @@ def test_split_call_matches_unsplit(monkeypatch):
     chain is the same fp32 arithmetic; the output of the first chunk after the split
     takes its state product in one piece instead of two."""
     x = W.prefill_inputs([8192] * 4, seed=13, gen_device="cuda", device="cuda")
+    monkeypatch.setenv("GDN_PREFILL_OVERLAP", "1")
+    if prefill.launches_per_call(4, 4 * 8192, 32) != 6:
+        pytest.skip("this GPU leaves fewer than 8 SMs idle for 128 chains: no split call")
     monkeypatch.setenv("GDN_PREFILL_OVERLAP", "0")
+    assert prefill.launches_per_call(4, 4 * 8192, 32) == 4
     o1, s1 = prefill.kernel(*x.args())
     monkeypatch.setenv("GDN_PREFILL_OVERLAP", "1")
     o2, s2 = prefill.kernel(*x.args())
@@ -173,13 +253,95 @@ def test_chunked_flags_bad_cu_seqlens_without_faulting():
     assert torch.equal(ns, state)
     prefill.reset_device_status()
     # out of range: [0, 700) with T = 640 is clamped to [0, 640)
+    ref_out, ref_ns = prefill.kernel(*x.args())
     args[8] = torch.tensor([0, 700], dtype=torch.int64, device="cuda")
     args[3] = x.state
     out, ns = prefill.kernel(*args)
-    ref_out, ref_ns = prefill.kernel(*x.args())
     torch.cuda.synchronize()
     assert prefill.device_status() & 2
     assert torch.equal(out, ref_out) and torch.equal(ns, ref_ns)
     prefill.reset_device_status()
     prefill.kernel(*x.args())
     assert prefill.device_status() == 0
+
+
+def test_chunked_failure_raises_through_python_entry():
+    """A failure the kernels report in the status word reaches the caller: with
+    check=True the failing call raises GDNError; without it the next call on the device
+    raises; reset_device_status() clears it, and a grown workspace keeps the bits."""
+    from flashinfer_bench_tma_thrust_b200._lib import GDNError
+    x = to_dev(W.prefill_inputs([640], HQ=2, HV=4, seed=5))
+    prefill.reset_device_status()
+    torch.cuda.synchronize()
+    # start from a fresh (small) workspace so that the big call below really grows it
+    prefill._workspaces.pop(("cuda", torch.cuda.current_device()), None)
+    args = list(x.args())
+    args[8] = torch.tensor([0, 700], dtype=torch.int64, device="cuda")  # T = 640
+    with pytest.raises(GDNError, match="status bits 0x2"):
+        prefill.kernel(*args, check=True)
+    with pytest.raises(GDNError):
+        prefill.kernel(*x.args())
+    prefill.reset_device_status()
+    prefill.kernel(*x.args(), check=True)
+    # a larger call grows the workspace: the sticky bit set before it survives
+    prefill.kernel(*args)
+    torch.cuda.synchronize()
+    big = to_dev(W.prefill_inputs([4096, 4096], HQ=2, HV=4, seed=6))
+    with pytest.raises(GDNError):
+        prefill.kernel(*big.args(), check=True)
+    assert prefill.device_status() & 2
+    prefill.reset_device_status()
+    prefill.kernel(*big.args(), check=True)
+    assert prefill.device_status() == 0
+
+
+def test_split_calls_from_two_host_threads():
+    """Two host threads call the C ABI at the same time on their own streams and
+    workspaces with split-call sizes (4 x 8192 tokens, 32 v-heads: the side stream and
+    its events are shared per device): every result equals the single-threaded one."""
+    import threading
+    from flashinfer_bench_tma_thrust_b200 import _checks as C, _lib
+    if prefill.launches_per_call(4, 4 * 8192, 32) != 6:
+        pytest.skip("no split call on this GPU for these sizes")
+    lib = _lib.load()
+    xs = [W.prefill_inputs([8192] * 4, seed=90 + i, gen_device="cuda", device="cuda")
+          for i in range(2)]
+    refs = [prefill.kernel(*x.args()) for x in xs]
+    torch.cuda.synchronize()
+    Ps = [prefill.prepare(*x.args()) for x in xs]
+    nb = lib.gdn_prefill_chunked_workspace_size(Ps[0].T, Ps[0].N, Ps[0].HV)
+    wss = [torch.zeros(nb, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    streams = [torch.cuda.Stream() for _ in range(2)]
+    results = [[None] * 6 for _ in range(2)]
+    errors = []
+    barrier = threading.Barrier(2)
+
+    def worker(i):
+        try:
+            P, st = Ps[i], streams[i]
+            barrier.wait()
+            for r in range(6):
+                with torch.cuda.stream(st):
+                    out, ns = prefill._alloc_outputs(P)
+                rc = lib.gdn_prefill_chunked_fwd(
+                    P.q.data_ptr(), P.k.data_ptr(), P.v.data_ptr(), C.ptr(P.state),
+                    P.A.data_ptr(), P.A_t, P.a.data_ptr(), P.a_t, P.d.data_ptr(), P.d_t,
+                    P.b.data_ptr(), P.b_t, P.cu.data_ptr(), P.cu_t, P.scale, out.data_ptr(),
+                    ns.data_ptr(), P.T, P.N, P.HQ, P.HV, P.D, wss[i].data_ptr(), nb,
+                    st.cuda_stream)
+                _lib.check(rc, "gdn_prefill_chunked_fwd")
+                results[i][r] = (out, ns)
+        except Exception as e:  # noqa: BLE001 - reported below
+            errors.append(e)
+
+    ths = [threading.Thread(target=worker, args=(i,)) for i in range(2)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    torch.cuda.synchronize()
+    assert not errors, errors
+    for i in range(2):
+        assert int(wss[i][:4].view(torch.int32).item()) == 0
+        for out, ns in results[i]:
+            assert torch.equal(out, refs[i][0]) and torch.equal(ns, refs[i][1])
