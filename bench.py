@@ -243,9 +243,10 @@ def reference_impl(op: str):
     return getattr(gdn_oracle, op), "port", f"oracle/gdn_oracle.py:{op} (restatement)"
 
 
-def cpu_decode_time(B_sample, steps, warmup, seed=1000):
-    """Time `steps` CPU decode steps of the reference implementation on the first
-    B_sample sequences of the B=256 workload (all host threads)."""
+def cpu_decode_time(B_sample, steps, warmup, seed=1000, min_seconds=0.0):
+    """Time `steps` CPU decode steps (more while under `min_seconds`) of the reference
+    implementation on the first B_sample sequences of the B=256 workload (all host
+    threads)."""
     from flashinfer_bench_tma_thrust_b200 import workloads as W
     fn, kind, where = reference_impl("decode")
     torch.set_num_threads(os.cpu_count() or 1)
@@ -254,9 +255,12 @@ def cpu_decode_time(B_sample, steps, warmup, seed=1000):
     for _ in range(warmup):
         fn(*sl)
     t0 = time.perf_counter()
-    for _ in range(steps):
+    n = 0
+    while n < steps or time.perf_counter() - t0 < min_seconds:
         fn(*sl)
+        n += 1
     el = time.perf_counter() - t0
+    steps = n
     sb = 2 * B_sample * HV * D * D * 4
     cores = torch.get_num_threads()
     return {"value": sb * steps / el / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
@@ -275,7 +279,8 @@ def decode_sample_size(steps, warmup, budget_s=150.0):
     return max(1, min(256, fit))
 
 
-def cpu_prefill_time(lengths, with_state, steps, warmup, tokens_per_seq=64, seed=2000):
+def cpu_prefill_time(lengths, with_state, steps, warmup, tokens_per_seq=64, seed=2000,
+                     min_seconds=0.0):
     """Time the reference implementation's prefill on the first `tokens_per_seq` tokens
     of each sequence of the configuration (same head layout and distributions)."""
     from flashinfer_bench_tma_thrust_b200 import workloads as W
@@ -286,9 +291,12 @@ def cpu_prefill_time(lengths, with_state, steps, warmup, tokens_per_seq=64, seed
     for _ in range(warmup):
         fn(*x.args())
     t0 = time.perf_counter()
-    for _ in range(steps):
+    n = 0
+    while n < steps or time.perf_counter() - t0 < min_seconds:
         fn(*x.args())
+        n += 1
     el = time.perf_counter() - t0
+    steps = n
     cores = torch.get_num_threads()
     return {"value": sum(sub) * steps / el, "unit": "tokens/s", "cores": cores, "kind": kind,
             "sample": f"first {tokens_per_seq} tokens of each of the {len(lengths)} sequences "
@@ -364,15 +372,19 @@ def run_ours(args, world, rank, local):
         if world == 1 and rank == 0 and not args.no_cpu_baseline:
             # the same implementation and inputs as the reference arm, on the full batch
             # when three steps fit in about 40 s
-            result["cpu_baseline"] = cpu_decode_time(decode_sample_size(3, 1, 40.0), 3, 1)[0]
+            result["cpu_baseline"] = cpu_decode_time(decode_sample_size(3, 1, 40.0), 3, 1,
+                                                     min_seconds=10.0)[0]
         if not args.no_extra:
             result["extra"] = {
                 "decode_bf16_state": decode_bf16_measure(x, info, K, Wm, device, world, ms_step),
                 "decode_fp8_state": decode_fp8_measure(x, info, K, Wm, device, world, ms_step)}
-            for w, k in (("prefill_varlen", 10), ("prefill_long", 5)):
+            for w, k, ke in (("prefill_varlen", 10, 10), ("prefill_long", 5, 4)):
                 result["extra"][w] = prefill_measure(w, k, 3, device, world, rank, pk, args,
-                                                     e2e_steps=3)
+                                                     e2e_steps=ke)
             result["extra"]["decode_sweep"] = decode_sweep_measure(device, world, rank)
+            if world == 1:
+                result["extra"]["reference_v10_decode"] = reference_v10_measure(
+                    x, info, device, ms_step)
     else:
         pm = prefill_measure(args.workload, K, Wm, device, world, rank, pk, args,
                              e2e_steps=min(K, 5))
@@ -437,6 +449,58 @@ def decode_sweep_measure(device, world, rank, batches=(1, 16, 64, 256, 1024, 409
             del g, keep, xs
         torch.cuda.empty_cache()
     return out
+
+
+def reference_v10_measure(x, info, device, our_ms_step, iters=50):
+    """Same-box comparator: the reference's own CUDA decode kernels ("v10", cute and tma
+    launchers of gdn/kernels/cute_cpp/gdn_decode_v10.cuh, built into oracle/_ref/) on
+    this run's B=256, 16/32-head inputs, for each BLOCK_V its launcher supports; the
+    state is ping-ponged between two buffers (a decode loop), CUDA events over `iters`
+    launches. Each launched configuration's first step is checked against ours."""
+    from oracle import ref_v10
+    from flashinfer_bench_tma_thrust_b200 import decode
+    if not ref_v10.available():
+        return {"unavailable": "oracle/_ref/libref_v10.so not built (no reference checkout)"}
+    B = info["B"]
+    out_ref, ns_ref = decode.kernel(*x.args())
+    rows = []
+    for variant, vname in ((0, "cute"), (1, "tma")):
+        for bv in (16, 32, 64):
+            o = torch.empty(B, HV, D, dtype=torch.bfloat16, device=device)
+            bufs = [x.state.clone(), torch.empty_like(x.state)]
+            rc = ref_v10.decode(x.q, x.k, x.v, bufs[0], x.A_log, x.a, x.dt_bias, x.b, o, bufs[1],
+                                x.scale, bv, variant)
+            torch.cuda.synchronize(device)
+            rec = {"launcher": vname, "BLOCK_V": bv, "launch_status": rc}
+            if rc == 0:
+                rec["max_abs_out_vs_ours"] = (o.float() - out_ref[:, 0].float()).abs().max().item()
+                rec["max_abs_state_vs_ours"] = (bufs[1] - ns_ref).abs().max().item()
+                for i in range(5):
+                    ref_v10.decode(x.q, x.k, x.v, bufs[i & 1], x.A_log, x.a, x.dt_bias, x.b, o,
+                                   bufs[(i + 1) & 1], x.scale, bv, variant)
+                torch.cuda.synchronize(device)
+                s = torch.cuda.Event(enable_timing=True)
+                e = torch.cuda.Event(enable_timing=True)
+                s.record()
+                for i in range(iters):
+                    ref_v10.decode(x.q, x.k, x.v, bufs[i & 1], x.A_log, x.a, x.dt_bias, x.b, o,
+                                   bufs[(i + 1) & 1], x.scale, bv, variant)
+                e.record()
+                e.synchronize()
+                ms = s.elapsed_time(e) / iters
+                rec.update({"ms_per_step": round(ms, 5),
+                            "state_gbs": round(info["state_bytes"] / (ms * 1e-3) / 1e9, 1)})
+            else:
+                rec["note"] = ("launch rejected: the launcher requests more dynamic shared "
+                               "memory than the 48 KB default without the opt-in attribute")
+            rows.append(rec)
+            del bufs
+    ok = [r for r in rows if r.get("ms_per_step")]
+    best = min(ok, key=lambda r: r["ms_per_step"]) if ok else None
+    return {"config": f"B={B}, 16 q/k heads, 32 v heads (this run's decode inputs)",
+            "runs": rows,
+            "best": {k: best[k] for k in ("launcher", "BLOCK_V", "state_gbs")} if best else None,
+            "ours_over_best": round(best["ms_per_step"] / our_ms_step, 3) if best else None}
 
 
 def decode_bf16_measure(x, info, K, Wm, device, world, fp32_ms_step):
@@ -561,10 +625,10 @@ def prefill_measure(workload, K, Wm, device, world, rank, pk, args, e2e_steps=3)
                       "l2": "inputs (q/k/v >= 100 MB) larger than L2; no flush"},
            "roofline": roof, "clocks": clocks, "gpu_launches": K * launches}
     if not args.no_e2e and jobs is not None:
-        out["e2e"] = e2e_measure(jobs, prefill.kernel, device, world, e2e_steps, 2,
+        out["e2e"] = e2e_measure(jobs, prefill.kernel, device, world, e2e_steps, 4,
                                  units=T_glob, scale=1.0, unit="tokens/s")
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_prefill_time(lengths, with_state, 3, 1)
+        out["cpu_baseline"] = cpu_prefill_time(lengths, with_state, 3, 1, min_seconds=10.0)
     return out
 
 

@@ -17,9 +17,12 @@
 // memory. Rows of one head are split over several thread blocks when the batch
 // is small so that all 148 SMs get work.
 #include <cuda_fp16.h>
+#include <algorithm>
+#include <cstdlib>
 
 #include "gdn_common.cuh"
 #include "gdn_launch.h"
+#include "sm100_umma.cuh"
 
 namespace gdn {
 
@@ -302,6 +305,178 @@ __global__ void __launch_bounds__(128) decode_fp8_kernel(DecodeParams p, const f
   }
 }
 
+
+// One head (128 rows) of the fp8 state in shared memory: codes, row scales, v.
+constexpr uint32_t kFp8Codes = kHeadDim * kHeadDim;         // 16384 bytes
+constexpr uint32_t kFp8StageBytes = kFp8Codes + 512 + 256;  // + 128 fp32 scales + 128 bf16 v
+constexpr int kFp8Stages = 2;
+constexpr uint32_t kFp8Smem = kFp8Stages * kFp8StageBytes + 64;
+
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Streaming fp8-state decode: a persistent block walks over heads (b, h) and keeps the
+// next head's codes, scales and v arriving in shared memory by bulk copy (one mbarrier
+// per stage) while it computes the current one, so that every SM has tens of KB of
+// loads in flight without holding them in registers. Warp w covers rows 32w..32w+31 in
+// 8 steps of 4 rows (lane = 8 sub + seg: 16 codes of row 4 step + sub per lane). The
+// row scale multiplies the two dot products once and the update's decay factor once
+// (S = c s: S.k = s (c.k), g S + d k = (g s) c + d k); products run as packed f32x2
+// operations. New codes, scales and outputs go straight to global memory. A bounded
+// wait that gives up marks that head's outputs and scales NaN and ends the block.
+template <bool HAS_STATE, int WARPS>
+__global__ void __launch_bounds__(32 * WARPS, WARPS == 4 ? 4 : 3) decode_fp8_stream_kernel(DecodeParams p,
+                                                                   const float* scale_in,
+                                                                   float* scale_out,
+                                                                   int64_t heads) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = sm100::align_smem<128>(smem_raw);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kFp8Stages * kFp8StageBytes);
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int sub = lane >> 3, seg = lane & 7;
+  const int64_t stride = gridDim.x;
+  const uint8_t* codes_g = static_cast<const uint8_t*>(p.state_any);
+  uint4* dst = static_cast<uint4*>(p.new_state_any);
+  if (t == 0) {
+    for (int s = 0; s < kFp8Stages; ++s) sm100::mbar_init(&bar[s], 1);
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int64_t hd, int s) {  // thread 0: head hd -> stage s
+    uint8_t* st = sm + s * kFp8StageBytes;
+    sm100::mbar_arrive_expect_tx(&bar[s], (HAS_STATE ? kFp8Codes + 512 : 0) + 256);
+    if (HAS_STATE) {
+      sm100::bulk_load(st, codes_g + hd * kFp8Codes, kFp8Codes, &bar[s]);
+      sm100::bulk_load(st + kFp8Codes, scale_in + hd * kHeadDim, 512, &bar[s]);
+    }
+    sm100::bulk_load(st + kFp8Codes + 512, p.v + hd * kHeadDim, 256, &bar[s]);
+  };
+  if (t == 0) {
+    for (int s = 0; s < kFp8Stages; ++s) {
+      const int64_t hd = blockIdx.x + s * stride;
+      if (hd < heads) issue(hd, s);
+    }
+  }
+  int it = 0;
+  for (int64_t head = blockIdx.x; head < heads; head += stride, ++it) {
+    const int s = it % kFp8Stages;
+    const uint32_t parity = static_cast<uint32_t>((it / kFp8Stages) & 1);
+    // per-head scalars and this lane's q/k segment while the copies land
+    const int64_t bi = head / p.HV;
+    const int h = static_cast<int>(head - bi * p.HV);
+    const int qh = h / (p.HV / p.HQ);
+    const float g = expf(gate_log_decay(load_scalar(p.A_log, p.A_log_dtype, h),
+                                        load_scalar(p.a, p.a_dtype, head),
+                                        load_scalar(p.dt_bias, p.dt_bias_dtype, h)));
+    const float beta = gate_beta(load_scalar(p.b, p.b_dtype, head));
+    const int64_t qk_off = (bi * p.HQ + qh) * kHeadDim + seg * 16;
+    float2 qf[8], kf[8];
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 q4 = load_bf16x4(p.q + qk_off + i), k4 = load_bf16x4(p.k + qk_off + i);
+      qf[i / 2] = make_float2(q4.x, q4.y);
+      qf[i / 2 + 1] = make_float2(q4.z, q4.w);
+      kf[i / 2] = make_float2(k4.x, k4.y);
+      kf[i / 2 + 1] = make_float2(k4.z, k4.w);
+    }
+    float2 kq2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) kq2 = sm100::fma2(qf[i], kf[i], kq2);
+    float kq = kq2.x + kq2.y;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
+    const bool ok = sm100::mbar_wait(&bar[s], parity);
+    if (!__all_sync(0xffffffffu, ok)) {
+      // the copies did not arrive: this head's results are marked invalid
+      if (lane < kHeadDim / WARPS) {
+        const int64_t row = head * kHeadDim + (kHeadDim / WARPS) * warp + lane;
+        scale_out[row] = __int_as_float(0x7fc00000);
+        p.out[row] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
+      }
+      break;
+    }
+    const uint8_t* st = sm + s * kFp8StageBytes;
+    const float* ssc = reinterpret_cast<const float*>(st + kFp8Codes);
+    const unsigned short* sv = reinterpret_cast<const unsigned short*>(st + kFp8Codes + 512);
+#pragma unroll 2
+    for (int step = 0; step < kHeadDim / (4 * WARPS); ++step) {
+      const int r = (kHeadDim / WARPS) * warp + 4 * step + sub;  // row within the head
+      const float vin = __uint_as_float(static_cast<uint32_t>(sv[r]) << 16);
+      float2 c[8];
+      float cs = 0.f;
+      if (HAS_STATE) {
+        const uint4 cw = *reinterpret_cast<const uint4*>(st + r * kHeadDim + seg * 16);
+        const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint32_t lo2, hi2;
+          asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+              "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+              : "=r"(lo2), "=r"(hi2)
+              : "r"(w[e]));
+          c[2 * e] = __half22float2(*reinterpret_cast<const __half2*>(&lo2));
+          c[2 * e + 1] = __half22float2(*reinterpret_cast<const __half2*>(&hi2));
+        }
+        cs = ssc[r];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) c[i] = make_float2(0.f, 0.f);
+      }
+      float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        sk2 = sm100::fma2(c[i], kf[i], sk2);
+        sq2 = sm100::fma2(c[i], qf[i], sq2);
+      }
+      float sk = sk2.x + sk2.y, sq = sq2.x + sq2.y;
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      }
+      sk *= cs;
+      sq *= cs;
+      const float delta = beta * (vin - g * sk);
+      const float gs = g * cs;
+      const float2 gs2 = make_float2(gs, gs), d2 = make_float2(delta, delta);
+      float m = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        c[i] = sm100::fma2(gs2, c[i], sm100::mul2(d2, kf[i]));
+        m = max3f(m, fabsf(c[i].x), fabsf(c[i].y));
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float nsc = m > 0.f ? m * (1.0f / 448.0f) : 1.0f;
+      const float inv = m > 0.f ? __fdividef(448.0f, m) : 1.0f;
+      uint32_t ow[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a = sm100::mul2(c[2 * e], make_float2(inv, inv));
+        const float2 b = sm100::mul2(c[2 * e + 1], make_float2(inv, inv));
+        uint16_t lo, hi;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(a.y), "f"(a.x));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(b.y), "f"(b.x));
+        ow[e] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      }
+      const int64_t row = head * kHeadDim + r;
+      asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(dst + row * 8 + seg),
+                   "r"(ow[0]), "r"(ow[1]), "r"(ow[2]), "r"(ow[3])
+                   : "memory");
+      if (seg == 0) {
+        scale_out[row] = nsc;
+        p.out[row] = __float2bfloat16_rn(p.scale * fmaf(g, sq, delta * kq));
+      }
+    }
+    __syncthreads();  // every warp is done with stage s
+    if (t == 0 && head + kFp8Stages * stride < heads) issue(head + kFp8Stages * stride, s);
+  }
+}
+
 }  // namespace
 
 int launch_decode_fp8(const DecodeParams& p_in, const float* scale_in, float* scale_out,
@@ -309,15 +484,42 @@ int launch_decode_fp8(const DecodeParams& p_in, const float* scale_in, float* sc
   DecodeParams p = p_in;
   const int64_t heads = p.B * p.HV;
   if (heads == 0) return 0;
-  int splits = 1;
-  while (splits < 8 && heads * splits < 148 * 4) splits *= 2;
-  p.splits = splits;
-  p.rows_per_warp = kHeadDim / (4 * splits);
-  const dim3 grid(static_cast<unsigned>(heads * splits));
-  if (p.rows_per_warp >= 16)
-    decode_fp8_kernel<4><<<grid, 128, 0, stream>>>(p, scale_in, scale_out);
-  else
-    decode_fp8_kernel<1><<<grid, 128, 0, stream>>>(p, scale_in, scale_out);
+  const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  const bool bulk_ok = a16(p.v) && (!p.state_any || (a16(p.state_any) && a16(scale_in)));
+  if (heads < 148 * 4 || !bulk_ok || getenv("GDN_FP8_V1")) {
+    // small batch: rows of a head split over several blocks so that all SMs get work
+    int splits = 1;
+    while (splits < 8 && heads * splits < 148 * 4) splits *= 2;
+    p.splits = splits;
+    p.rows_per_warp = kHeadDim / (4 * splits);
+    const dim3 grid(static_cast<unsigned>(heads * splits));
+    if (p.rows_per_warp >= 16)
+      decode_fp8_kernel<4><<<grid, 128, 0, stream>>>(p, scale_in, scale_out);
+    else
+      decode_fp8_kernel<1><<<grid, 128, 0, stream>>>(p, scale_in, scale_out);
+  } else {
+    // persistent streaming blocks, as many as fit on the GPU at once
+    static int blocks_per_sm[4] = {0, 0, 0, 0}, sms = 0;
+    const bool has = p.state_any != nullptr;
+    const bool w8 = getenv("GDN_FP8_W8") != nullptr;
+    const int nthr = w8 ? 256 : 128;
+    auto fn = has ? (w8 ? decode_fp8_stream_kernel<true, 8> : decode_fp8_stream_kernel<true, 4>)
+                  : (w8 ? decode_fp8_stream_kernel<false, 8> : decode_fp8_stream_kernel<false, 4>);
+    const int key = has + 2 * w8;
+    if (!blocks_per_sm[key]) {
+      int dev = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+          cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kFp8Smem + 128) !=
+              cudaSuccess ||
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm[key], fn, nthr,
+                                                        kFp8Smem + 128) != cudaSuccess)
+        return -1;
+    }
+    const int64_t grid = std::min<int64_t>(heads, static_cast<int64_t>(sms) * blocks_per_sm[key]);
+    fn<<<static_cast<unsigned>(grid), nthr, kFp8Smem + 128, stream>>>(p, scale_in, scale_out,
+                                                                      heads);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

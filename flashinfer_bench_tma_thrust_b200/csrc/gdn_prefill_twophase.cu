@@ -569,7 +569,7 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
   uint64_t* bar_g3 = bar_kq + 8;    //          G3
   uint64_t* bar_g1a = bar_kq + 9;   //          G1a
   uint64_t* bar_x = bar_kq + 10;    // state warps: X^T stored
-  uint64_t* bar_op = bar_kq + 11;   //              S operand stored
+  uint64_t* bar_op = bar_kq + 11;   //              S operand stored, B_c read
   uint64_t* bar_u = bar_kq + 12;    //              U'^T stored
   uint64_t* bar_bi = bar_kq + 13;   //              B_c image stored
   uint64_t* bar_o = bar_kq + 14;    //              chunk's output rows read
@@ -893,16 +893,19 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         // every state thread has read dS_{c-1}
         if (!named_bar_and(kStateBar, kScanWState, ok)) break;
         tc_fence_after();
-        write_s_operand(g_prev);
-        signal(bar_op);
         ok = mbar_wait(bar_tb, ph_tb) && ok;
         ph_tb ^= 1;
         tc_fence_after();
         {
-          // row v of B_c^T (the [K;Q]_{c+1} row), columns i in [16c, 16c+16)
+          // row v of B_c^T (the [K;Q]_{c+1} row), columns i in [16c, 16c+16). B_c sits in
+          // the (QH)^T half of D1_{c+1}'s buffer, which G1a_{c+1} overwrites: the operand
+          // is signalled (and G1a_{c+1} issued) only once every thread holds its B_c row.
+          // The load runs while the operand is converted and stored.
           float bt[16];
           tmem_ld16(lane + d1n + 64 + 16 * ch, bt);
+          write_s_operand(g_prev);
           tmem_ld_wait();
+          signal(bar_op);
           uint32_t hw[8], lw[8];
           split_words<8>(bt, hw, lw);
           uint8_t* bimg = sm + Q_OFF_B;

@@ -341,7 +341,14 @@ def test_split_calls_from_two_host_threads():
         t.join()
     torch.cuda.synchronize()
     assert not errors, errors
+    bad = []
     for i in range(2):
         assert int(wss[i][:4].view(torch.int32).item()) == 0
-        for out, ns in results[i]:
-            assert torch.equal(out, refs[i][0]) and torch.equal(ns, refs[i][1])
+        for r, (out, ns) in enumerate(results[i]):
+            if not (torch.equal(out, refs[i][0]) and torch.equal(ns, refs[i][1])):
+                dif = (out != refs[i][0]).any(-1).nonzero()
+                bad.append((i, r, (out.float() - refs[i][0].float()).abs().max().item(),
+                            (ns - refs[i][1]).abs().max().item(), int(dif.shape[0]),
+                            dif[:6].tolist()))
+    assert not bad, ("(thread, call, max |out diff|, max |state diff|, differing (token, "
+                     f"head) rows, first ones): {bad}")
