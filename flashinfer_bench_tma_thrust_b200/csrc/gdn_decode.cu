@@ -328,8 +328,8 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 // (S = c s: S.k = s (c.k), g S + d k = (g s) c + d k); products run as packed f32x2
 // operations. New codes, scales and outputs go straight to global memory. A bounded
 // wait that gives up marks that head's outputs and scales NaN and ends the block.
-template <bool HAS_STATE, int WARPS>
-__global__ void __launch_bounds__(32 * WARPS, WARPS == 4 ? 4 : 3) decode_fp8_stream_kernel(DecodeParams p,
+template <bool HAS_STATE>
+__global__ void __launch_bounds__(128, 4) decode_fp8_stream_kernel(DecodeParams p,
                                                                    const float* scale_in,
                                                                    float* scale_out,
                                                                    int64_t heads) {
@@ -392,8 +392,8 @@ __global__ void __launch_bounds__(32 * WARPS, WARPS == 4 ? 4 : 3) decode_fp8_str
     const bool ok = sm100::mbar_wait(&bar[s], parity);
     if (!__all_sync(0xffffffffu, ok)) {
       // the copies did not arrive: this head's results are marked invalid
-      if (lane < kHeadDim / WARPS) {
-        const int64_t row = head * kHeadDim + (kHeadDim / WARPS) * warp + lane;
+      if (lane < kHeadDim / 4) {
+        const int64_t row = head * kHeadDim + (kHeadDim / 4) * warp + lane;
         scale_out[row] = __int_as_float(0x7fc00000);
         p.out[row] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
       }
@@ -403,8 +403,8 @@ __global__ void __launch_bounds__(32 * WARPS, WARPS == 4 ? 4 : 3) decode_fp8_str
     const float* ssc = reinterpret_cast<const float*>(st + kFp8Codes);
     const unsigned short* sv = reinterpret_cast<const unsigned short*>(st + kFp8Codes + 512);
 #pragma unroll 2
-    for (int step = 0; step < kHeadDim / (4 * WARPS); ++step) {
-      const int r = (kHeadDim / WARPS) * warp + 4 * step + sub;  // row within the head
+    for (int step = 0; step < kHeadDim / 16; ++step) {
+      const int r = (kHeadDim / 4) * warp + 4 * step + sub;  // row within the head
       const float vin = __uint_as_float(static_cast<uint32_t>(sv[r]) << 16);
       float2 c[8];
       float cs = 0.f;
@@ -441,17 +441,21 @@ __global__ void __launch_bounds__(32 * WARPS, WARPS == 4 ? 4 : 3) decode_fp8_str
       sk *= cs;
       sq *= cs;
       const float delta = beta * (vin - g * sk);
-      const float gs = g * cs;
-      const float2 gs2 = make_float2(gs, gs), d2 = make_float2(delta, delta);
+      // new row n = (g s) c + d k = gs (c + r k) with r = d / gs: one packed FMA per
+      // pair; gs is kept >= 1e-30 (a smaller one changes n by at most 1e-30 |c|), and the
+      // row maximum and the quantisation scale carry the factor gs
+      const float gs = fmaxf(g * cs, 1e-30f);
+      const float rr = __fdividef(delta, gs);
+      const float2 r2 = make_float2(rr, rr);
       float m = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        c[i] = sm100::fma2(gs2, c[i], sm100::mul2(d2, kf[i]));
+        c[i] = sm100::fma2(r2, kf[i], c[i]);
         m = max3f(m, fabsf(c[i].x), fabsf(c[i].y));
       }
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const float nsc = m > 0.f ? m * (1.0f / 448.0f) : 1.0f;
+      const float nsc = m > 0.f ? gs * m * (1.0f / 448.0f) : 1.0f;
       const float inv = m > 0.f ? __fdividef(448.0f, m) : 1.0f;
       uint32_t ow[4];
 #pragma unroll
@@ -499,13 +503,11 @@ int launch_decode_fp8(const DecodeParams& p_in, const float* scale_in, float* sc
       decode_fp8_kernel<1><<<grid, 128, 0, stream>>>(p, scale_in, scale_out);
   } else {
     // persistent streaming blocks, as many as fit on the GPU at once
-    static int blocks_per_sm[4] = {0, 0, 0, 0}, sms = 0;
+    static int blocks_per_sm[2] = {0, 0}, sms = 0;
     const bool has = p.state_any != nullptr;
-    const bool w8 = getenv("GDN_FP8_W8") != nullptr;
-    const int nthr = w8 ? 256 : 128;
-    auto fn = has ? (w8 ? decode_fp8_stream_kernel<true, 8> : decode_fp8_stream_kernel<true, 4>)
-                  : (w8 ? decode_fp8_stream_kernel<false, 8> : decode_fp8_stream_kernel<false, 4>);
-    const int key = has + 2 * w8;
+    const int nthr = 128;
+    auto fn = has ? decode_fp8_stream_kernel<true> : decode_fp8_stream_kernel<false>;
+    const int key = has;
     if (!blocks_per_sm[key]) {
       int dev = 0;
       if (cudaGetDevice(&dev) != cudaSuccess ||

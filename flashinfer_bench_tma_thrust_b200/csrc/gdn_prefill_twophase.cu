@@ -893,17 +893,16 @@ __global__ void __launch_bounds__(kScanWThreads, 1)
         // every state thread has read dS_{c-1}
         if (!named_bar_and(kStateBar, kScanWState, ok)) break;
         tc_fence_after();
+        write_s_operand(g_prev);
         ok = mbar_wait(bar_tb, ph_tb) && ok;
         ph_tb ^= 1;
         tc_fence_after();
         {
           // row v of B_c^T (the [K;Q]_{c+1} row), columns i in [16c, 16c+16). B_c sits in
           // the (QH)^T half of D1_{c+1}'s buffer, which G1a_{c+1} overwrites: the operand
-          // is signalled (and G1a_{c+1} issued) only once every thread holds its B_c row.
-          // The load runs while the operand is converted and stored.
+          // is signalled (and G1a_{c+1} issued) only once every thread holds its B_c row
           float bt[16];
           tmem_ld16(lane + d1n + 64 + 16 * ch, bt);
-          write_s_operand(g_prev);
           tmem_ld_wait();
           signal(bar_op);
           uint32_t hw[8], lw[8];
