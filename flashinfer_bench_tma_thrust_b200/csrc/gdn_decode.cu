@@ -308,7 +308,8 @@ __global__ void __launch_bounds__(128) decode_fp8_kernel(DecodeParams p, const f
 
 // One head (128 rows) of the fp8 state in shared memory: codes, row scales, v.
 constexpr uint32_t kFp8Codes = kHeadDim * kHeadDim;         // 16384 bytes
-constexpr uint32_t kFp8StageBytes = kFp8Codes + 512 + 256;  // + 128 fp32 scales + 128 bf16 v
+// + 128 fp32 scales, 128 bf16 v, the head's q and k rows (128 bf16 each)
+constexpr uint32_t kFp8StageBytes = kFp8Codes + 512 + 256 + 512;
 constexpr int kFp8Stages = 2;
 constexpr uint32_t kFp8Smem = kFp8Stages * kFp8StageBytes + 64;
 
@@ -348,13 +349,25 @@ __global__ void __launch_bounds__(128, 4) decode_fp8_stream_kernel(DecodeParams 
   __syncthreads();
   auto issue = [&](int64_t hd, int s) {  // thread 0: head hd -> stage s
     uint8_t* st = sm + s * kFp8StageBytes;
-    sm100::mbar_arrive_expect_tx(&bar[s], (HAS_STATE ? kFp8Codes + 512 : 0) + 256);
+    sm100::mbar_arrive_expect_tx(&bar[s], (HAS_STATE ? kFp8Codes + 512 : 0) + 768);
     if (HAS_STATE) {
       sm100::bulk_load(st, codes_g + hd * kFp8Codes, kFp8Codes, &bar[s]);
       sm100::bulk_load(st + kFp8Codes, scale_in + hd * kHeadDim, 512, &bar[s]);
     }
     sm100::bulk_load(st + kFp8Codes + 512, p.v + hd * kHeadDim, 256, &bar[s]);
+    const int64_t qrow = (hd / p.HV * p.HQ + (hd % p.HV) / (p.HV / p.HQ)) * kHeadDim;
+    sm100::bulk_load(st + kFp8Codes + 768, p.q + qrow, 256, &bar[s]);
+    sm100::bulk_load(st + kFp8Codes + 1024, p.k + qrow, 256, &bar[s]);
   };
+  // the gate inputs of the block's first head; later heads' are loaded one head ahead
+  float ga = 0.f, gb = 0.f, gA = 0.f, gd = 0.f;
+  if (static_cast<int64_t>(blockIdx.x) < heads) {
+    const int h0 = static_cast<int>(blockIdx.x % p.HV);
+    ga = load_scalar(p.a, p.a_dtype, blockIdx.x);
+    gb = load_scalar(p.b, p.b_dtype, blockIdx.x);
+    gA = load_scalar(p.A_log, p.A_log_dtype, h0);
+    gd = load_scalar(p.dt_bias, p.dt_bias_dtype, h0);
+  }
   if (t == 0) {
     for (int s = 0; s < kFp8Stages; ++s) {
       const int64_t hd = blockIdx.x + s * stride;
@@ -365,23 +378,39 @@ __global__ void __launch_bounds__(128, 4) decode_fp8_stream_kernel(DecodeParams 
   for (int64_t head = blockIdx.x; head < heads; head += stride, ++it) {
     const int s = it % kFp8Stages;
     const uint32_t parity = static_cast<uint32_t>((it / kFp8Stages) & 1);
-    // per-head scalars and this lane's q/k segment while the copies land
-    const int64_t bi = head / p.HV;
-    const int h = static_cast<int>(head - bi * p.HV);
-    const int qh = h / (p.HV / p.HQ);
-    const float g = expf(gate_log_decay(load_scalar(p.A_log, p.A_log_dtype, h),
-                                        load_scalar(p.a, p.a_dtype, head),
-                                        load_scalar(p.dt_bias, p.dt_bias_dtype, h)));
-    const float beta = gate_beta(load_scalar(p.b, p.b_dtype, head));
-    const int64_t qk_off = (bi * p.HQ + qh) * kHeadDim + seg * 16;
+    const float g = expf(gate_log_decay(gA, ga, gd));
+    const float beta = gate_beta(gb);
+    {  // the next head's gate inputs, consumed one iteration later
+      const int64_t nh = head + stride;
+      if (nh < heads) {
+        const int h1 = static_cast<int>(nh % p.HV);
+        ga = load_scalar(p.a, p.a_dtype, nh);
+        gb = load_scalar(p.b, p.b_dtype, nh);
+        gA = load_scalar(p.A_log, p.A_log_dtype, h1);
+        gd = load_scalar(p.dt_bias, p.dt_bias_dtype, h1);
+      }
+    }
+    const bool ok = sm100::mbar_wait(&bar[s], parity);
+    if (!__all_sync(0xffffffffu, ok)) {
+      // the copies did not arrive: this head's results are marked invalid
+      const int64_t row = head * kHeadDim + (kHeadDim / 4) * warp + lane;
+      scale_out[row] = __int_as_float(0x7fc00000);
+      p.out[row] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
+      break;
+    }
+    // this lane's q/k segment from the stage
+    const uint8_t* stq = sm + s * kFp8StageBytes + kFp8Codes + 768;
     float2 qf[8], kf[8];
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      const float4 q4 = load_bf16x4(p.q + qk_off + i), k4 = load_bf16x4(p.k + qk_off + i);
-      qf[i / 2] = make_float2(q4.x, q4.y);
-      qf[i / 2 + 1] = make_float2(q4.z, q4.w);
-      kf[i / 2] = make_float2(k4.x, k4.y);
-      kf[i / 2 + 1] = make_float2(k4.z, k4.w);
+    for (int i = 0; i < 2; ++i) {
+      const uint4 qw = *reinterpret_cast<const uint4*>(stq + seg * 32 + 16 * i);
+      const uint4 kw = *reinterpret_cast<const uint4*>(stq + 256 + seg * 32 + 16 * i);
+      const uint32_t qa[4] = {qw.x, qw.y, qw.z, qw.w}, ka[4] = {kw.x, kw.y, kw.z, kw.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        qf[4 * i + e] = make_float2(__uint_as_float(qa[e] << 16), __uint_as_float(qa[e] & 0xffff0000u));
+        kf[4 * i + e] = make_float2(__uint_as_float(ka[e] << 16), __uint_as_float(ka[e] & 0xffff0000u));
+      }
     }
     float2 kq2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -389,16 +418,6 @@ __global__ void __launch_bounds__(128, 4) decode_fp8_stream_kernel(DecodeParams 
     float kq = kq2.x + kq2.y;
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
-    const bool ok = sm100::mbar_wait(&bar[s], parity);
-    if (!__all_sync(0xffffffffu, ok)) {
-      // the copies did not arrive: this head's results are marked invalid
-      if (lane < kHeadDim / 4) {
-        const int64_t row = head * kHeadDim + (kHeadDim / 4) * warp + lane;
-        scale_out[row] = __int_as_float(0x7fc00000);
-        p.out[row] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
-      }
-      break;
-    }
     const uint8_t* st = sm + s * kFp8StageBytes;
     const float* ssc = reinterpret_cast<const float*>(st + kFp8Codes);
     const unsigned short* sv = reinterpret_cast<const unsigned short*>(st + kFp8Codes + 512);
@@ -489,7 +508,8 @@ int launch_decode_fp8(const DecodeParams& p_in, const float* scale_in, float* sc
   const int64_t heads = p.B * p.HV;
   if (heads == 0) return 0;
   const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-  const bool bulk_ok = a16(p.v) && (!p.state_any || (a16(p.state_any) && a16(scale_in)));
+  const bool bulk_ok = a16(p.v) && a16(p.q) && a16(p.k) &&
+                       (!p.state_any || (a16(p.state_any) && a16(scale_in)));
   if (heads < 148 * 4 || !bulk_ok || getenv("GDN_FP8_V1")) {
     // small batch: rows of a head split over several blocks so that all SMs get work
     int splits = 1;
