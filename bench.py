@@ -323,6 +323,19 @@ def run_ours(args, world, rank, local):
     K, Wm = args.steps, args.warmup
     result = {"n_gpus": world, "steps": K, "warmup": Wm, "higher_is_better": True,
               "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
+    if args.workload == "decode_fp8":
+        # the reduced-precision option alone (a separately reported figure; used for its
+        # ncu summary): fp8 E4M3 state + row scales, B per GPU as the decode workload
+        b0, b1 = plan_decode(args.batch * world, world)[rank]
+        x, info = decode_workload(device, seed=1000 + b0, B=b1 - b0)
+        sampler = ClockSampler(device)
+        fp = decode_fp8_measure(x, info, K, Wm, device, world, float("nan"))
+        result.update({"metric": "GDN decode fp8-state GB/s (fp8 state + row scales / step time)",
+                       "value": fp["value"], "unit": "GB/s", "ms_per_step": fp["ms_per_step"],
+                       "dtype": "fp8 e4m3 state, f32 math", "clocks": sampler.stop(),
+                       "config": {"workload": f"gdn_decode fp8 state B={args.batch}/GPU"},
+                       "gpu_launches": K, "frac_of_hbm": fp["frac_of_hbm"]})
+        return result
     if args.workload == "decode":
         # the global batch (B per GPU x world) sharded by sequence with the partitioner
         B_glob = args.batch * world
@@ -664,10 +677,16 @@ def e2e_measure(jobs, fn, device, world, K, Wm, units, scale, unit):
         free[j].record(comp)
         drained[j].record(s_out)
     it = [0]
+    held = [None, None]  # each set's last results, kept until their copy-out is done
 
     def step():
         j = it[0] % 2
         it[0] += 1
+        if held[j] is not None:
+            # the results of two steps ago leave the host's hands only once copied out,
+            # so the allocator can reuse their memory without a stream-use record
+            drained[j].synchronize()
+            held[j] = None
         with torch.cuda.stream(s_in):
             s_in.wait_event(free[j])
             for dst_a, src_a in zip(dev_sets[j], host_sets[j]):
@@ -684,9 +703,9 @@ def e2e_measure(jobs, fn, device, world, K, Wm, units, scale, unit):
             s_out.wait_event(done[j])
             for res, res_h in zip(results, outs_h[j]):
                 for o, oh in zip(res, res_h):
-                    o.record_stream(s_out)
                     oh.copy_(o, non_blocking=True)
             drained[j].record(s_out)
+        held[j] = results
 
     for _ in range(Wm):
         step()
@@ -758,7 +777,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill_varlen", "prefill_long"])
+                    choices=["decode", "decode_fp8", "prefill_varlen", "prefill_long"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=256, help="decode sequences per GPU")
     ap.add_argument("--no-e2e", action="store_true")

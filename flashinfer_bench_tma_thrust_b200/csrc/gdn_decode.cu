@@ -445,13 +445,16 @@ __global__ void __launch_bounds__(128, 4) decode_fp8_stream_kernel(DecodeParams 
 #pragma unroll
         for (int i = 0; i < 8; ++i) c[i] = make_float2(0.f, 0.f);
       }
-      float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
+      // two independent accumulator chains per dot product (instruction-level parallelism)
+      float2 sk2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      float2 sq2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        sk2 = sm100::fma2(c[i], kf[i], sk2);
-        sq2 = sm100::fma2(c[i], qf[i], sq2);
+        sk2[i & 1] = sm100::fma2(c[i], kf[i], sk2[i & 1]);
+        sq2[i & 1] = sm100::fma2(c[i], qf[i], sq2[i & 1]);
       }
-      float sk = sk2.x + sk2.y, sq = sq2.x + sq2.y;
+      float sk = (sk2[0].x + sk2[0].y) + (sk2[1].x + sk2[1].y);
+      float sq = (sq2[0].x + sq2[0].y) + (sq2[1].x + sq2[1].y);
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) {
         sk += __shfl_xor_sync(0xffffffffu, sk, o);
@@ -466,12 +469,13 @@ __global__ void __launch_bounds__(128, 4) decode_fp8_stream_kernel(DecodeParams 
       const float gs = fmaxf(g * cs, 1e-30f);
       const float rr = __fdividef(delta, gs);
       const float2 r2 = make_float2(rr, rr);
-      float m = 0.f;
+      float mm[2] = {0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         c[i] = sm100::fma2(r2, kf[i], c[i]);
-        m = max3f(m, fabsf(c[i].x), fabsf(c[i].y));
+        mm[i & 1] = max3f(mm[i & 1], fabsf(c[i].x), fabsf(c[i].y));
       }
+      float m = fmaxf(mm[0], mm[1]);
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       const float nsc = m > 0.f ? gs * m * (1.0f / 448.0f) : 1.0f;
@@ -510,7 +514,7 @@ int launch_decode_fp8(const DecodeParams& p_in, const float* scale_in, float* sc
   const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   const bool bulk_ok = a16(p.v) && a16(p.q) && a16(p.k) &&
                        (!p.state_any || (a16(p.state_any) && a16(scale_in)));
-  if (heads < 148 * 4 || !bulk_ok || getenv("GDN_FP8_V1")) {
+  if (heads < 148 * 4 || !bulk_ok) {
     // small batch: rows of a head split over several blocks so that all SMs get work
     int splits = 1;
     while (splits < 8 && heads * splits < 148 * 4) splits *= 2;
