@@ -295,21 +295,26 @@ def test_chunked_failure_raises_through_python_entry():
     assert prefill.device_status() == 0
 
 
-def test_split_calls_from_two_host_threads():
+@pytest.mark.parametrize("path", ["two_phase", "fused"])
+def test_split_calls_from_two_host_threads(path):
     """Two host threads call the C ABI at the same time on their own streams and
-    workspaces with split-call sizes (4 x 8192 tokens, 32 v-heads: the side stream and
-    its events are shared per device): every result equals the single-threaded one."""
+    workspaces, every result compared bit for bit with the single-threaded one. Two-phase
+    path: split-call sizes (4 x 8192 tokens, 32 v-heads; the side stream and its events
+    are shared per device). Fused path (a 256-byte workspace): the same inputs. Timing
+    differences between concurrent calls expose hand-off races inside a kernel."""
     import threading
     from flashinfer_bench_tma_thrust_b200 import _checks as C, _lib
-    if prefill.launches_per_call(4, 4 * 8192, 32) != 6:
+    if path == "two_phase" and prefill.launches_per_call(4, 4 * 8192, 32) != 6:
         pytest.skip("no split call on this GPU for these sizes")
     lib = _lib.load()
     xs = [W.prefill_inputs([8192] * 4, seed=90 + i, gen_device="cuda", device="cuda")
           for i in range(2)]
-    refs = [prefill.kernel(*x.args()) for x in xs]
+    ref_fn = prefill.kernel if path == "two_phase" else prefill.kernel_fused
+    refs = [ref_fn(*x.args()) for x in xs]
     torch.cuda.synchronize()
     Ps = [prefill.prepare(*x.args()) for x in xs]
-    nb = lib.gdn_prefill_chunked_workspace_size(Ps[0].T, Ps[0].N, Ps[0].HV)
+    nb = (lib.gdn_prefill_chunked_workspace_size(Ps[0].T, Ps[0].N, Ps[0].HV)
+          if path == "two_phase" else 256)
     wss = [torch.zeros(nb, dtype=torch.uint8, device="cuda") for _ in range(2)]
     streams = [torch.cuda.Stream() for _ in range(2)]
     results = [[None] * 6 for _ in range(2)]
