@@ -81,6 +81,16 @@ def _qk(shape, g, gen_device, dist):
 
 
 def _params(HV, lead, g, gen_device, dist, gate_dtype):
+    if dist == "slowdecay":
+        # the benchmark distributions with exp(A_log) ~ U(0.001, 0.05) instead of U(1, 16):
+        # per-token decay g ~ 0.99, so the state survives many 64-token chunks (with the
+        # benchmark's gates it decays to zero in fp32 within one chunk)
+        A_log = torch.log(torch.rand(HV, generator=g, device=gen_device) * 0.049 + 0.001)
+        dt_bias = torch.rand(HV, generator=g, device=gen_device) * 2.0 - 1.0
+        a = torch.randn(*lead, HV, generator=g, device=gen_device)
+        b = torch.randn(*lead, HV, generator=g, device=gen_device)
+        gd = gate_dtype or torch.bfloat16
+        return A_log.float(), a.to(gd), dt_bias.float(), b.to(gd)
     if dist == "baseline":
         A_log = torch.log(torch.rand(HV, generator=g, device=gen_device) * 15.0 + 1.0)
         dt_bias = torch.rand(HV, generator=g, device=gen_device) * 2.0 - 1.0
@@ -99,7 +109,7 @@ def _params(HV, lead, g, gen_device, dist, gate_dtype):
 def decode_inputs(B, HQ=HQ_FULL, HV=HV_FULL, seed=0, device="cpu", gen_device="cpu",
                   dist="baseline", with_state=True, gate_dtype=None) -> DecodeInputs:
     g = _gen(seed, gen_device)
-    if dist == "baseline":
+    if dist in ("baseline", "slowdecay"):
         q = _qk((B, 1, HQ, D), g, gen_device, dist)
         k = _qk((B, 1, HQ, D), g, gen_device, dist)
         v = torch.randn(B, 1, HV, D, generator=g, device=gen_device)
@@ -124,7 +134,7 @@ def prefill_inputs(lengths, HQ=HQ_FULL, HV=HV_FULL, seed=0, device="cpu", gen_de
     g = _gen(seed, gen_device)
     T = int(sum(lengths))
     N = len(lengths)
-    if dist == "baseline":
+    if dist in ("baseline", "slowdecay"):
         q = _qk((T, HQ, D), g, gen_device, dist)
         k = _qk((T, HQ, D), g, gen_device, dist)
         v = torch.randn(T, HV, D, generator=g, device=gen_device)

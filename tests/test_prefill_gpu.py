@@ -12,6 +12,9 @@ from parity import (PREFILL_STATE_ATOL, STATE_REL_FROB, assert_out_close, assert
 pytestmark = pytest.mark.gpu
 
 PRE_CASES = [c for c in golden.case_names() if c.startswith("pre_")]
+IMPLS = {"chunked": prefill.kernel, "fused": prefill.kernel_fused,
+         "recurrent": prefill.kernel_recurrent}
+
 
 def _report(name, out, ref_out, ns, ref_ns, extra=None):
     """Append the parity figures of a full-size case to $GDN_PARITY_REPORT (JSON lines)
@@ -51,6 +54,44 @@ def test_chunked_vs_oracle_varlen_config():
     assert prefill.device_status() == 0
 
 
+SLOW_LENGTHS = [[1000, 130, 0, 2048, 64], [129, 192, 193, 256], [4097]]
+
+
+@pytest.mark.parametrize("impl", sorted(IMPLS))
+@pytest.mark.parametrize("lengths", SLOW_LENGTHS, ids=lambda l: "-".join(map(str, l)))
+def test_prefill_slow_decay_vs_oracle(lengths, impl):
+    """Gates with slow decay (g ~ 0.98 per token: the state carries across many 64-token
+    chunks; with the benchmark's gates it decays to zero in fp32 within one chunk, so
+    the inter-chunk state products would go untested), initial state N(0, 0.02)."""
+    x = W.prefill_inputs(lengths, seed=len(lengths) + 7, dist="slowdecay")
+    ref_out, ref_ns = gdn_oracle.prefill(*x.args())
+    out, ns = IMPLS[impl](*to_dev(x).args())
+    torch.cuda.synchronize()
+    _report(f"slowdecay_{impl}_{'-'.join(map(str, lengths))}", out, ref_out, ns, ref_ns)
+    assert_out_close(out, ref_out, f"slow decay {lengths}, {impl}")
+    assert_state_close(ns, ref_ns, PREFILL_STATE_ATOL, f"slow decay {lengths}, {impl}")
+
+
+def test_prefill_slow_decay_split_call_vs_oracle(monkeypatch):
+    """Slow-decay gates through the split-call path (4 x 8192 tokens, 32 v-heads: the
+    second scan part starts from the states the first wrote, which now matter), against
+    the oracle on the first and the last sequence."""
+    monkeypatch.delenv("GDN_PREFILL_OVERLAP", raising=False)
+    lengths = [8192] * 4
+    x = W.prefill_inputs(lengths, seed=11, dist="slowdecay")
+    if prefill.launches_per_call(4, sum(lengths), 32) != 6:
+        pytest.skip("no split call on this GPU for these sizes")
+    out, ns = prefill.kernel(*to_dev(x).args())
+    torch.cuda.synchronize()
+    for n in (0, 3):
+        xs, s0, e0 = _seq_slice(x, n)
+        ref_out, ref_ns = gdn_oracle.prefill(*xs.args())
+        _report(f"slowdecay_split_seq{n}", out[s0:e0], ref_out, ns[n:n + 1], ref_ns)
+        assert_out_close(out[s0:e0], ref_out, f"slow decay split, sequence {n}")
+        assert_state_close(ns[n:n + 1], ref_ns, PREFILL_STATE_ATOL,
+                           f"slow decay split, sequence {n}")
+
+
 def _seq_slice(x, n):
     """Inputs of sequence n of a packed prefill input alone (cu_seqlens [0, L])."""
     import dataclasses
@@ -88,8 +129,6 @@ def test_chunked_vs_oracle_long_config_split(monkeypatch):
                            f"long config, sequence {n} vs oracle")
     assert prefill.device_status() == 0
 
-IMPLS = {"chunked": prefill.kernel, "fused": prefill.kernel_fused,
-         "recurrent": prefill.kernel_recurrent}
 
 
 @pytest.mark.parametrize("impl", sorted(IMPLS))
