@@ -31,9 +31,10 @@ def test_bf16_state_single_step(B):
     assert ((got - ref_state).abs() <= tol).all()
 
 
-def test_bf16_state_error_over_100_steps():
+@pytest.mark.parametrize("dist", ["baseline", "slowdecay"])
+def test_bf16_state_error_over_100_steps(dist):
     B, steps = 8, 100
-    x = to_dev(W.decode_inputs(B, seed=7))
+    x = to_dev(W.decode_inputs(B, seed=7, dist=dist))
     s32 = x.state.clone()
     s16 = x.state.to(torch.bfloat16)
     g = torch.Generator(device="cuda").manual_seed(1)
@@ -51,4 +52,6 @@ def test_bf16_state_error_over_100_steps():
     state_rel = ((s16.float() - s32).norm() / s32.norm()).item()
     print(f"bf16 state, {steps} steps: max output rel err {max_out_rel:.2e}, "
           f"final state rel err {state_rel:.2e}")
-    assert state_rel < 1e-2 and max_out_rel < 2e-2
+    # measured on B200: 1.7e-3 / 1.0e-3 (benchmark gates), 9.2e-3 / 9.6e-3 (slow decay)
+    bound = 1e-2 if dist == "baseline" else 2e-2
+    assert state_rel < bound and max_out_rel < 2e-2

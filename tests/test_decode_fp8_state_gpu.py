@@ -35,9 +35,10 @@ def test_fp8_state_single_step(B):
     assert ((got - ref_state).abs() <= step * 0.5 + 1e-7).float().mean() > 0.999
 
 
-def test_fp8_state_error_over_100_steps():
+@pytest.mark.parametrize("dist", ["baseline", "slowdecay"])
+def test_fp8_state_error_over_100_steps(dist):
     B, steps = 8, 100
-    x = to_dev(W.decode_inputs(B, seed=9))
+    x = to_dev(W.decode_inputs(B, seed=9, dist=dist))
     s32 = x.state.clone()
     codes, sc = decode.quantize_state_fp8(x.state)
     g = torch.Generator(device="cuda").manual_seed(2)
@@ -57,4 +58,7 @@ def test_fp8_state_error_over_100_steps():
     state_rel = ((s8 - s32).norm() / s32.norm()).item()
     print(f"fp8 state, {steps} steps: max output rel err {max_out_rel:.2e}, "
           f"final state rel err {state_rel:.2e}")
-    assert state_rel < 0.1 and max_out_rel < 0.1
+    # measured on B200: 2.7e-2 / 1.1e-2 (benchmark gates), 0.127 / 0.127 (slow decay: the
+    # state keeps ~0.98 of itself per step, so each step's requantisation error persists)
+    bound = 0.1 if dist == "baseline" else 0.2
+    assert state_rel < bound and max_out_rel < bound
