@@ -1,6 +1,7 @@
 """Benchmark of the GDN hot path on B200 — prints ONE JSON line (rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill_varlen|prefill_long]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload decode|decode_fp8|prefill_varlen|prefill_long]
                     [--impl ours|reference]
 
 Workloads (seeded synthetic inputs with the benchmark configurations' shapes and
@@ -17,6 +18,8 @@ distributions; the reference's official trace dataset is not available):
   split into (sequence, head-group) units over the ranks (strong scaling).
 * ``prefill_long``: 4 sequences x 32768 tokens per GPU, zero initial state (32 x 32768
   on 8 GPUs). Metric: tokens/s.
+* ``decode_fp8``: the fp8-state option alone (B=256 per GPU), a separately reported
+  figure (GB/s of fp8 state + row scales).
 
 The decode run (the default) also reports both prefill configurations, the bf16 and
 fp8 state options and the decode batch sweep under ``extra``, each with its own

@@ -18,7 +18,6 @@
 // is small so that all 148 SMs get work.
 #include <cuda_fp16.h>
 #include <algorithm>
-#include <cstdlib>
 
 #include "gdn_common.cuh"
 #include "gdn_launch.h"
